@@ -1,0 +1,113 @@
+"""ctypes binding of libafterimage_b200.so (the C ABI in
+include/afterimage_b200.h).
+
+The library is built in-tree (afterimage_b200/lib/) by
+afterimage_b200.csrc.build; if it is missing, it is built on first use with
+nvcc. There is no fallback: if the library cannot be loaded every decode
+entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import threading
+
+from .csrc import build as _build
+
+_lock = threading.Lock()
+_lib = None
+
+AIB_OK = 0
+AIB_EINVAL = 1
+AIB_ECUDA = 2
+AIB_MAX_BATCH = 16
+
+STATUS_BAD_CHUNK_RANGE = 1
+STATUS_LUT_NOT_PREFIX = 2
+STATUS_LUT_RANGE = 4
+STATUS_WAIT_TIMEOUT = 8
+
+P = ctypes.c_void_p
+I64 = ctypes.c_int64
+I32 = ctypes.c_int32
+CI = ctypes.c_int
+
+
+class StreamDesc(ctypes.Structure):
+    """aib_stream_desc (include/afterimage_b200.h)."""
+    _fields_ = [
+        ("packed", P),
+        ("packed_capacity", I64),
+        ("packed_nbytes", I64),
+        ("offset_base", I64),
+        ("chunk_offsets", P),
+        ("chunk_nbytes", P),
+        ("chunk_base", I64),
+        ("tables", P),
+        ("sym_lut", P),
+        ("len_lut", P),
+        ("max_bits", I32),
+        ("chunk_size", I32),
+        ("n_symbols", I64),
+        ("elem_begin", I64),
+        ("elem_end", I64),
+        ("sign_mantissa", P),
+        ("out", P),
+    ]
+
+
+# (name, restype, argtypes) of every exported entry point; tests check that
+# the header declares exactly these.
+SIGNATURES = [
+    ("aib_last_error", ctypes.c_char_p, []),
+    ("aib_abi_version", CI, []),
+    ("aib_split_bf16", CI, [P, I64, P, P]),
+    ("aib_histogram", CI, [P, I64, P]),
+    ("aib_build_code", CI, [P, CI, P, P, P]),
+    ("aib_build_decode_lut", CI, [P, P, CI, P, P]),
+    ("aib_chunk_nbytes", CI, [P, I64, I64, P, P, P]),
+    ("aib_pack_chunks", CI, [P, I64, I64, P, P, P, P, P, I64]),
+    ("aib_host_threads", CI, []),
+    ("aib_tables_bytes", ctypes.c_size_t, []),
+    ("aib_build_tables", CI, [P, P, CI, P, P]),
+    ("aib_tables_flags", CI, [P, P, P]),
+    ("aib_decode_bf16", CI, [ctypes.POINTER(StreamDesc), P, P]),
+    ("aib_decode_exponents_u8", CI, [ctypes.POINTER(StreamDesc), P, P]),
+    ("aib_decode_exponents_i32", CI, [ctypes.POINTER(StreamDesc), P, P]),
+    ("aib_decode_bf16_batch", CI, [ctypes.POINTER(StreamDesc), CI, P, P]),
+    ("aib_recombine", CI, [P, P, I64, P, P]),
+]
+
+
+class AibError(RuntimeError):
+    pass
+
+
+def lib_path() -> pathlib.Path:
+    return _build.LIB
+
+
+def load():
+    """Load (building if needed) the library; raises if that fails."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            path = _build.build()
+            L = ctypes.CDLL(str(path))
+            for name, res, args in SIGNATURES:
+                fn = getattr(L, name)
+                fn.restype = res
+                fn.argtypes = args
+            if L.aib_abi_version() != 1:
+                raise AibError("libafterimage_b200.so ABI version mismatch")
+            _lib = L
+    return _lib
+
+
+def check(rc: int, what: str = "") -> None:
+    if rc == AIB_OK:
+        return
+    msg = load().aib_last_error().decode(errors="replace")
+    if rc == AIB_EINVAL:
+        raise ValueError(f"{what}: {msg}" if what else msg)
+    raise AibError(f"{what}: {msg}" if what else msg)

@@ -1,0 +1,669 @@
+// sm_100a kernels for the lossless BF16 weight-decode path, plus their C ABI.
+//
+// Format (reference: afterimage/runtime/huffman_chunked.py:135-207): the
+// exponent stream of a tensor is split into chunks of `chunk_size` symbols;
+// chunk c is an MSB-first canonical-Huffman bitstream, byte aligned, at byte
+// chunk_offsets[c] of `packed`. The reference decoder (ChunkedBitReader,
+// huffman_chunked.py:210-244; Triton kernel gpu_decode_v2.py:27-68) looks up
+// sym_lut/len_lut with the next max_bits bits, emits one symbol and consumes
+// its length.
+//
+// Kernel design (one launch decodes any number of whole or partial tensors):
+//   * one chunk per lane, 32 consecutive chunks per warp ("group");
+//   * a 12-bit first-level table, built once per tensor from the reference
+//     LUTs (aib_build_tables), staged into shared memory with one TMA bulk
+//     copy per CTA. An entry holds up to four symbols whose codes fit
+//     entirely inside the 12 bits, with their total length; codes longer
+//     than that (rare: the table covers every code of <= 12 bits) take an
+//     exact slow path through the reference LUT in global memory, so every
+//     decoded symbol equals the reference's LUT result;
+//   * each lane streams its chunk's bytes through a register queue of
+//     16-byte aligned loads into a 64-bit bit buffer;
+//   * symbols are flushed four at a time into a per-lane shared-memory
+//     ring; every 64 symbols the warp merges the ring with the sign/mantissa
+//     bytes (the reference's _recombine, compressed_store.py:94-114) and
+//     writes 16-byte vectorised BF16 stores, 128 contiguous bytes per chunk.
+// The decoder uses no tensor cores and no scratch global memory: the
+// exponent never round-trips through HBM.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "aib_internal.h"
+
+// ---------------------------------------------------------------------------
+// error plumbing
+// ---------------------------------------------------------------------------
+static thread_local char g_err[512] = "";
+
+void aib_set_error(const char *msg) { std::snprintf(g_err, sizeof(g_err), "%s", msg); }
+
+void aib_set_errorf(const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  std::vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+#define AIB_CUDA(call)                                                          \
+  do {                                                                          \
+    cudaError_t e_ = (call);                                                    \
+    if (e_ != cudaSuccess) {                                                    \
+      aib_set_errorf("%s: %s (%s)", __func__, cudaGetErrorString(e_), #call);  \
+      return AIB_ECUDA;                                                         \
+    }                                                                           \
+  } while (0)
+
+namespace aib {
+
+constexpr int kFastBits = 12;
+constexpr int kFastSize = 1 << kFastBits;
+constexpr int kFastBytes = kFastSize * 8;
+constexpr int kTablesBytes = kFastBytes + 16;  // fast table + {flags, max_bits, pad}
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kPhase = 64;        // symbols per lane between merges
+constexpr int kRing = 128;        // ring bytes per lane (power of two >= kPhase + 11)
+constexpr int kRow = kRing + 8;   // padded row: lanes at equal k hit different banks
+constexpr int kRingWarpBytes = 32 * kRow;
+constexpr int kSmemBytes = kFastBytes + kWarps * kRingWarpBytes;
+constexpr unsigned kWaitLimit = 1u << 22;  // bounded mbarrier wait (~0.3 s with backoff)
+
+enum Mode { kModeBF16 = 0, kModeU8 = 1, kModeI32 = 2 };
+
+struct Job {
+  const uint8_t *packed;
+  int64_t packed_cap;
+  int64_t packed_nbytes;
+  int64_t offset_base;
+  const int32_t *offs;    // entry c - chunk_base describes chunk c
+  const int32_t *nbytes;
+  int64_t chunk_base;
+  const uint2 *fast;
+  const int32_t *flags;
+  const int32_t *sym_lut;
+  const int8_t *len_lut;
+  const uint8_t *sm;
+  void *out;
+  int64_t n_symbols;
+  int64_t e0, e1;
+  int64_t c_begin, c_end;  // covering chunk range
+  int64_t n_groups;        // ceil((c_end - c_begin) / 32)
+  int32_t max_bits;
+  int32_t chunk_size;
+  int32_t cta_begin;
+  int32_t ctas;
+  int32_t vec_ok;
+  int32_t pad;
+};
+
+struct Batch {
+  Job job[AIB_MAX_BATCH];
+  int32_t count;
+};
+
+// ---------------------------------------------------------------------------
+// device helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+// 1-D TMA bulk copy global -> this CTA's shared memory (no multicast).
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, unsigned bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint4 ld_blk(const uint4 *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint32_t bswap(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
+
+__device__ __forceinline__ uint2 slow_entry(uint64_t acc, const int32_t *__restrict__ sym_lut,
+                                            const int8_t *__restrict__ len_lut, int max_bits) {
+  // the reference LUT lookup itself: window = next max_bits bits
+  const uint32_t w = (static_cast<uint32_t>(acc >> 48)) >> (16 - max_bits);
+  const uint32_t s = static_cast<uint32_t>(__ldg(sym_lut + w)) & 0xFFu;
+  const uint32_t l = static_cast<uint32_t>(static_cast<int>(__ldg(len_lut + w))) & 0xFFu;
+  return make_uint2(s, 1u | (l << 8));
+}
+
+// 8 exponents + 8 sign/mantissa bytes -> 8 bf16 (bits = s<<15 | e<<7 | m).
+__device__ __forceinline__ uint4 combine8(uint2 ex, uint2 sm) {
+  const uint32_t M = 0x807F807Fu;
+  uint4 o;
+  o.x = (__byte_perm(ex.x, 0, 0x4140) << 7) | (__byte_perm(sm.x, 0, 0x1100) & M);
+  o.y = (__byte_perm(ex.x, 0, 0x4342) << 7) | (__byte_perm(sm.x, 0, 0x3322) & M);
+  o.z = (__byte_perm(ex.y, 0, 0x4140) << 7) | (__byte_perm(sm.y, 0, 0x1100) & M);
+  o.w = (__byte_perm(ex.y, 0, 0x4342) << 7) | (__byte_perm(sm.y, 0, 0x3322) & M);
+  return o;
+}
+
+__device__ __forceinline__ uint16_t combine1(uint32_t e, uint32_t sm) {
+  return static_cast<uint16_t>((e << 7) | (sm & 0x7Fu) | ((sm & 0x80u) << 8));
+}
+
+// ---------------------------------------------------------------------------
+// table construction (prepare_decode_tables)
+// ---------------------------------------------------------------------------
+__global__ void validate_lut_kernel(const int32_t *__restrict__ sym_lut, const int8_t *__restrict__ len_lut,
+                                    int max_bits, int32_t *flags) {
+  const int size = 1 << max_bits;
+  int bad = 0;
+  for (int w = blockIdx.x * blockDim.x + threadIdx.x; w < size; w += gridDim.x * blockDim.x) {
+    const int s = sym_lut[w];
+    const int l = len_lut[w];
+    if (s < 0 || s > 255 || l < 0 || l > max_bits) {
+      bad |= AIB_STATUS_LUT_RANGE;
+    } else if (l > 0) {
+      // a prefix-code LUT repeats an entry across every window sharing the
+      // code's l leading bits (huffman.py:140-148)
+      const int base = w & ~((1 << (max_bits - l)) - 1);
+      if (sym_lut[base] != s || len_lut[base] != l) bad |= AIB_STATUS_LUT_NOT_PREFIX;
+    }
+  }
+  if (bad) atomicOr(flags, bad);
+}
+
+__global__ void build_fast_kernel(const int32_t *__restrict__ sym_lut, const int8_t *__restrict__ len_lut,
+                                  int max_bits, uint2 *fast, int32_t *header) {
+  const int v = blockIdx.x * blockDim.x + threadIdx.x;
+  if (v == 0) header[1] = max_bits;
+  if (v >= kFastSize) return;
+  const uint32_t mask = (max_bits >= 32) ? 0xFFFFFFFFu : ((1u << max_bits) - 1u);
+  uint32_t syms = 0;
+  int cnt = 0, p = 0;
+  while (cnt < 4) {
+    uint32_t w;
+    bool full;
+    if (p + max_bits <= kFastBits) {
+      w = (static_cast<uint32_t>(v) >> (kFastBits - p - max_bits)) & mask;
+      full = true;
+    } else {
+      const int known = kFastBits - p;  // bits of v left; the rest of the window is unknown
+      const uint32_t kbits = known > 0 ? (static_cast<uint32_t>(v) & ((1u << known) - 1u)) : 0u;
+      w = kbits << (max_bits - known);
+      full = false;
+    }
+    const int s = sym_lut[w];
+    const int l = len_lut[w];
+    // a partially known window is decided only when its code lies entirely
+    // inside the known bits (a prefix code is fixed by its leading bits)
+    if (!full && !(l >= 1 && l <= kFastBits - p)) break;
+    if (l < 0 || l > 16) break;
+    syms |= (static_cast<uint32_t>(s) & 0xFFu) << (8 * cnt);
+    ++cnt;
+    p += l;
+  }
+  fast[v] = make_uint2(syms, static_cast<uint32_t>(cnt) | (static_cast<uint32_t>(p) << 8));
+}
+
+// ---------------------------------------------------------------------------
+// the decode kernel
+// ---------------------------------------------------------------------------
+template <int MODE>
+__global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ Batch batch,
+                                                          int32_t *status) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t bar;
+
+  int jsel = 0;
+  for (int t = 1; t < batch.count; ++t)
+    if (static_cast<int>(blockIdx.x) >= batch.job[t].cta_begin) jsel = t;
+  const Job &J = batch.job[jsel];
+
+  uint2 *s_fast = reinterpret_cast<uint2 *>(smem);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_expect_tx(&bar, kFastBytes);
+    bulk_g2s(s_fast, J.fast, kFastBytes, &bar);
+  }
+  __syncthreads();
+  {
+    unsigned spins = 0;
+    bool timed_out = false;
+    while (!mbar_try_wait(&bar, 0)) {
+      if (++spins > kWaitLimit) {
+        timed_out = true;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (timed_out) {
+      if (status) atomicOr(status, AIB_STATUS_WAIT_TIMEOUT);
+      return;
+    }
+  }
+  const bool force_slow = (*J.flags) != 0;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  unsigned char *ring_base = smem + kFastBytes + warp * kRingWarpBytes;
+  unsigned char *my_ring = ring_base + lane * kRow;
+  const int64_t cs = J.chunk_size;
+  const int max_bits = J.max_bits;
+  const uint4 *src = reinterpret_cast<const uint4 *>(J.packed);
+  const int64_t bmax = J.packed_cap / 16 - 1;
+
+  for (int64_t grp = static_cast<int64_t>(blockIdx.x - J.cta_begin) * kWarps + warp; grp < J.n_groups;
+       grp += static_cast<int64_t>(J.ctas) * kWarps) {
+    const int64_t c0 = J.c_begin + grp * 32;
+    const int64_t c = c0 + lane;
+    const bool active = c < J.c_end;
+    const int64_t chunk_e0 = c * cs;
+    const int need = active ? static_cast<int>(min(cs, J.e1 - chunk_e0)) : 0;
+
+    // ---- bit reader set-up -------------------------------------------------
+    uint64_t acc = 0;
+    int nb = 0;
+    uint4 q = make_uint4(0, 0, 0, 0), nxt = make_uint4(0, 0, 0, 0);
+    int qn = 4;
+    int64_t bi = 0;
+    if (active) {
+      int64_t pos = static_cast<int64_t>(J.offs[c - J.chunk_base]) - J.offset_base;
+      const int64_t nbyt = J.nbytes[c - J.chunk_base];
+      if (pos < 0 || nbyt < 0 || pos + nbyt > J.packed_nbytes) {
+        if (status) atomicOr(status, AIB_STATUS_BAD_CHUNK_RANGE);
+        pos = 0;
+      }
+      bi = pos >> 4;
+      const uint4 b0 = ld_blk(src + min(bi, bmax));
+      nxt = ld_blk(src + min(bi + 1, bmax));
+      bi += 2;
+      q = make_uint4(bswap(b0.x), bswap(b0.y), bswap(b0.z), bswap(b0.w));
+      const int wofs = static_cast<int>((pos >> 2) & 3);
+      if (wofs & 2) q = make_uint4(q.z, q.w, q.x, q.y);
+      if (wofs & 1) q = make_uint4(q.y, q.z, q.w, q.x);
+      qn = 4 - wofs;
+      // first word, then drop the bytes before the chunk start
+      acc = static_cast<uint64_t>(q.x) << 32;
+      nb = 32;
+      q.x = q.y; q.y = q.z; q.z = q.w;
+      if (--qn == 0) {
+        q = make_uint4(bswap(nxt.x), bswap(nxt.y), bswap(nxt.z), bswap(nxt.w));
+        qn = 4;
+        nxt = ld_blk(src + min(bi, bmax));
+        ++bi;
+      }
+      const int skip = static_cast<int>(pos & 3) * 8;
+      acc <<= skip;
+      nb -= skip;
+    }
+
+    const int max_need = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(need));
+    int k = 0;     // symbols flushed to the ring (multiple of 4)
+    int nout = 0;  // symbols pending in outacc
+    uint64_t outacc = 0;
+
+    for (int ph = 0; ph < max_need; ph += kPhase) {
+      const int target = min(ph + kPhase, need);
+      while (k + nout < target) {
+        if (nb < 32) {
+          acc |= static_cast<uint64_t>(q.x) << (32 - nb);
+          nb += 32;
+          q.x = q.y; q.y = q.z; q.z = q.w;
+          if (--qn == 0) {
+            q = make_uint4(bswap(nxt.x), bswap(nxt.y), bswap(nxt.z), bswap(nxt.w));
+            qn = 4;
+            nxt = ld_blk(src + min(bi, bmax));
+            ++bi;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          uint2 e = s_fast[static_cast<uint32_t>(acc >> (64 - kFastBits))];
+          if (force_slow || (e.y & 7u) == 0u) e = slow_entry(acc, J.sym_lut, J.len_lut, max_bits);
+          const uint32_t used = e.y >> 8;
+          acc <<= used;
+          nb -= static_cast<int>(used);
+          outacc |= static_cast<uint64_t>(e.x) << (8 * nout);
+          nout += static_cast<int>(e.y & 7u);
+          if (nout >= 4) {
+            *reinterpret_cast<uint32_t *>(my_ring + (k & (kRing - 1))) = static_cast<uint32_t>(outacc);
+            outacc >>= 32;
+            nout -= 4;
+            k += 4;
+          }
+        }
+      }
+      if (k < target)  // end of this lane's range: flush the partial word
+        *reinterpret_cast<uint32_t *>(my_ring + (k & (kRing - 1))) = static_cast<uint32_t>(outacc);
+      __syncwarp();
+
+      // ---- merge: 32 chunks x kPhase symbols, 8 elements per lane-step ------
+#pragma unroll 2
+      for (int it = 0; it < kPhase * 32 / 8 / 32; ++it) {
+        const int r = it * 4 + (lane >> 3);
+        const int q8 = (lane & 7) * 8;
+        const int64_t cr = c0 + r;
+        if (cr >= J.c_end) continue;
+        const int64_t base = cr * cs;
+        const int64_t lo = max(base, J.e0);
+        const int64_t hi = min(base + cs, J.e1);
+        const int64_t g = base + ph + q8;
+        if (g >= hi || g + 8 <= lo) continue;
+        const unsigned char *rrow = ring_base + r * kRow;
+        const int ro = (ph + q8) & (kRing - 1);
+        const int64_t oi = g - J.e0;
+        if (J.vec_ok && g >= lo && g + 8 <= hi) {
+          const uint2 ex = *reinterpret_cast<const uint2 *>(rrow + ro);
+          if (MODE == kModeBF16) {
+            const uint2 smv = __ldcs(reinterpret_cast<const uint2 *>(J.sm + oi));
+            __stcs(reinterpret_cast<uint4 *>(static_cast<uint16_t *>(J.out) + oi), combine8(ex, smv));
+          } else if (MODE == kModeU8) {
+            __stcs(reinterpret_cast<uint2 *>(static_cast<uint8_t *>(J.out) + oi), ex);
+          } else {
+            uint4 a, b;
+            a.x = __byte_perm(ex.x, 0, 0x4440); a.y = __byte_perm(ex.x, 0, 0x4441);
+            a.z = __byte_perm(ex.x, 0, 0x4442); a.w = __byte_perm(ex.x, 0, 0x4443);
+            b.x = __byte_perm(ex.y, 0, 0x4440); b.y = __byte_perm(ex.y, 0, 0x4441);
+            b.z = __byte_perm(ex.y, 0, 0x4442); b.w = __byte_perm(ex.y, 0, 0x4443);
+            int32_t *o = static_cast<int32_t *>(J.out) + oi;
+            __stcs(reinterpret_cast<uint4 *>(o), a);
+            __stcs(reinterpret_cast<uint4 *>(o + 4), b);
+          }
+        } else {
+          for (int jj = 0; jj < 8; ++jj) {
+            const int64_t gg = g + jj;
+            if (gg < lo || gg >= hi) continue;
+            const uint32_t e = rrow[(ro + jj) & (kRing - 1)];
+            const int64_t o = gg - J.e0;
+            if (MODE == kModeBF16)
+              static_cast<uint16_t *>(J.out)[o] = combine1(e, J.sm[o]);
+            else if (MODE == kModeU8)
+              static_cast<uint8_t *>(J.out)[o] = static_cast<uint8_t>(e);
+            else
+              static_cast<int32_t *>(J.out)[o] = static_cast<int32_t>(e);
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+}
+
+__global__ void recombine_kernel(const uint8_t *__restrict__ e, const uint8_t *__restrict__ sm, int64_t n,
+                                 uint16_t *__restrict__ out, int vec) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (vec) {
+    const int64_t nv = n / 8;
+    for (int64_t v = i; v < nv; v += stride) {
+      const uint2 ex = __ldcs(reinterpret_cast<const uint2 *>(e) + v);
+      const uint2 s = __ldcs(reinterpret_cast<const uint2 *>(sm) + v);
+      __stcs(reinterpret_cast<uint4 *>(out) + v, combine8(ex, s));
+    }
+    for (int64_t t = nv * 8 + i; t < n; t += stride) out[t] = combine1(e[t], sm[t]);
+  } else {
+    for (int64_t t = i; t < n; t += stride) out[t] = combine1(e[t], sm[t]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+struct DeviceInfo {
+  int sms = 0;
+  int occ[3] = {0, 0, 0};
+  bool ready = false;
+};
+static DeviceInfo g_dev[64];
+static std::mutex g_dev_mu;
+
+template <int MODE>
+static int setup_kernel(int dev, DeviceInfo &di) {
+  AIB_CUDA(cudaFuncSetAttribute(decode_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  int occ = 0;
+  AIB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<MODE>, kThreads, kSmemBytes));
+  di.occ[MODE] = std::max(1, occ);
+  return AIB_OK;
+}
+
+static int device_info(DeviceInfo **out) {
+  int dev = 0;
+  AIB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) {
+    aib_set_error("device index out of range");
+    return AIB_EINVAL;
+  }
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo &di = g_dev[dev];
+  if (!di.ready) {
+    AIB_CUDA(cudaDeviceGetAttribute(&di.sms, cudaDevAttrMultiProcessorCount, dev));
+    int rc;
+    if ((rc = setup_kernel<kModeBF16>(dev, di)) != AIB_OK) return rc;
+    if ((rc = setup_kernel<kModeU8>(dev, di)) != AIB_OK) return rc;
+    if ((rc = setup_kernel<kModeI32>(dev, di)) != AIB_OK) return rc;
+    di.ready = true;
+  }
+  *out = &di;
+  return AIB_OK;
+}
+
+static bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+// Fills a Job from a descriptor; returns AIB_OK, or AIB_EINVAL with the
+// message set. *empty is set when there is nothing to produce.
+static int make_job(const aib_stream_desc *d, int mode, Job *j, bool *empty) {
+  if (!d) {
+    aib_set_error("null descriptor");
+    return AIB_EINVAL;
+  }
+  *empty = false;
+  if (d->chunk_size < 1) return aib_set_errorf("chunk_size must be >= 1, got %d", d->chunk_size), AIB_EINVAL;
+  if (d->max_bits < 0 || d->max_bits > 16)
+    return aib_set_errorf("max_bits must be in [0, 16], got %d", d->max_bits), AIB_EINVAL;
+  if (d->n_symbols < 0 || d->elem_begin < 0 || d->elem_end < d->elem_begin || d->elem_end > d->n_symbols)
+    return aib_set_errorf("bad element range [%lld, %lld) for %lld symbols", (long long)d->elem_begin,
+                          (long long)d->elem_end, (long long)d->n_symbols),
+           AIB_EINVAL;
+  if (d->elem_end == d->elem_begin) {
+    *empty = true;
+    return AIB_OK;
+  }
+  const int64_t n_chunks = (d->n_symbols + d->chunk_size - 1) / d->chunk_size;
+  if (n_chunks > INT32_MAX) return aib_set_error("too many chunks for int32 chunk indices"), AIB_EINVAL;
+  if (!d->packed || !aligned(d->packed, 16)) return aib_set_error("packed must be a 16-byte aligned device pointer"), AIB_EINVAL;
+  if (d->packed_capacity < 16 || (d->packed_capacity & 15) || d->packed_nbytes < 0 ||
+      d->packed_nbytes > d->packed_capacity)
+    return aib_set_errorf("packed_capacity %lld must be a multiple of 16, >= 16 and >= packed_nbytes %lld",
+                          (long long)d->packed_capacity, (long long)d->packed_nbytes),
+           AIB_EINVAL;
+  if (!d->chunk_offsets || !d->chunk_nbytes || !d->tables || !d->sym_lut || !d->len_lut || !d->out)
+    return aib_set_error("null device pointer in descriptor"), AIB_EINVAL;
+  if (!aligned(d->tables, 16)) return aib_set_error("tables must be 16-byte aligned"), AIB_EINVAL;
+  if (mode == kModeBF16 && !d->sign_mantissa) return aib_set_error("sign_mantissa is required"), AIB_EINVAL;
+  if (!aligned(d->out, mode == kModeBF16 ? 2 : (mode == kModeI32 ? 4 : 1)))
+    return aib_set_error("out is misaligned for its element type"), AIB_EINVAL;
+
+  j->packed = d->packed;
+  j->packed_cap = d->packed_capacity;
+  j->packed_nbytes = d->packed_nbytes;
+  j->offset_base = d->offset_base;
+  j->offs = d->chunk_offsets;
+  j->nbytes = d->chunk_nbytes;
+  j->chunk_base = d->chunk_base;
+  j->fast = static_cast<const uint2 *>(d->tables);
+  j->flags = reinterpret_cast<const int32_t *>(static_cast<const unsigned char *>(d->tables) + kFastBytes);
+  j->sym_lut = d->sym_lut;
+  j->len_lut = d->len_lut;
+  j->sm = d->sign_mantissa;
+  j->out = d->out;
+  j->n_symbols = d->n_symbols;
+  j->e0 = d->elem_begin;
+  j->e1 = d->elem_end;
+  j->chunk_size = d->chunk_size;
+  j->max_bits = d->max_bits;
+  j->c_begin = d->elem_begin / d->chunk_size;
+  j->c_end = (d->elem_end + d->chunk_size - 1) / d->chunk_size;
+  j->n_groups = (j->c_end - j->c_begin + 31) / 32;
+  if (d->chunk_base < 0 || d->chunk_base > j->c_begin)
+    return aib_set_errorf("chunk_base %lld must be in [0, %lld]", (long long)d->chunk_base,
+                          (long long)j->c_begin),
+           AIB_EINVAL;
+  const bool base_ok = (d->chunk_size % 8 == 0) && (d->elem_begin % 8 == 0);
+  if (mode == kModeBF16)
+    j->vec_ok = base_ok && aligned(d->out, 16) && aligned(d->sign_mantissa, 8);
+  else if (mode == kModeU8)
+    j->vec_ok = base_ok && aligned(d->out, 8);
+  else
+    j->vec_ok = base_ok && aligned(d->out, 16);
+  j->pad = 0;
+  return AIB_OK;
+}
+
+// groups of 32 chunks handled per warp before a CTA is considered full
+static constexpr int kGroupsPerWarp = 2;
+
+template <int MODE>
+static int launch(const aib_stream_desc *descs, int count, int32_t *status, void *stream) {
+  if (count < 1 || count > AIB_MAX_BATCH) {
+    aib_set_errorf("batch count must be in [1, %d], got %d", AIB_MAX_BATCH, count);
+    return AIB_EINVAL;
+  }
+  if (!descs) return aib_set_error("null descriptor array"), AIB_EINVAL;
+  // validate every descriptor on the host before touching the device
+  Batch batch;
+  std::memset(&batch, 0, sizeof(batch));
+  int64_t total_groups = 0;
+  int n = 0;
+  int rc = AIB_OK;
+  for (int i = 0; i < count; ++i) {
+    bool empty = false;
+    rc = make_job(&descs[i], MODE, &batch.job[n], &empty);
+    if (rc != AIB_OK) return rc;
+    if (empty) continue;
+    total_groups += batch.job[n].n_groups;
+    ++n;
+  }
+  if (n == 0) return AIB_OK;
+  DeviceInfo *di = nullptr;
+  rc = device_info(&di);
+  if (rc != AIB_OK) return rc;
+  batch.count = n;
+  // CTAs: as many as the work needs at kGroupsPerWarp groups per warp, capped
+  // at a few full waves; split across jobs in proportion to their groups.
+  const int64_t wave = static_cast<int64_t>(di->sms) * di->occ[MODE];
+  const int64_t want = (total_groups + kWarps * kGroupsPerWarp - 1) / (kWarps * kGroupsPerWarp);
+  const int64_t cap = std::max<int64_t>(want, 1) < 4 * wave ? std::max<int64_t>(want, 1) : 4 * wave;
+  int cta = 0;
+  for (int i = 0; i < n; ++i) {
+    Job &j = batch.job[i];
+    int64_t share = (cap * j.n_groups + total_groups - 1) / total_groups;
+    const int64_t max_useful = (j.n_groups + kWarps - 1) / kWarps;
+    share = std::max<int64_t>(1, std::min(share, max_useful));
+    j.cta_begin = cta;
+    j.ctas = static_cast<int32_t>(share);
+    cta += j.ctas;
+  }
+  decode_kernel<MODE><<<cta, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(batch, status);
+  AIB_CUDA(cudaGetLastError());
+  return AIB_OK;
+}
+
+}  // namespace aib
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+using namespace aib;
+
+AIB_API const char *aib_last_error(void) { return g_err; }
+AIB_API int aib_abi_version(void) { return 1; }
+AIB_API size_t aib_tables_bytes(void) { return kTablesBytes; }
+
+AIB_API int aib_build_tables(const int32_t *d_sym_lut, const int8_t *d_len_lut, int max_bits, void *d_tables,
+                             void *stream) {
+  if (!d_sym_lut || !d_len_lut || !d_tables) return aib_set_error("aib_build_tables: null pointer"), AIB_EINVAL;
+  if (max_bits < 0 || max_bits > 16) return aib_set_errorf("aib_build_tables: max_bits %d not in [0, 16]", max_bits), AIB_EINVAL;
+  if (!aligned(d_tables, 16)) return aib_set_error("aib_build_tables: tables must be 16-byte aligned"), AIB_EINVAL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned char *base = static_cast<unsigned char *>(d_tables);
+  int32_t *header = reinterpret_cast<int32_t *>(base + kFastBytes);
+  AIB_CUDA(cudaMemsetAsync(header, 0, 16, s));
+  const int lut = 1 << max_bits;
+  validate_lut_kernel<<<std::min(64, (lut + 255) / 256), 256, 0, s>>>(d_sym_lut, d_len_lut, max_bits, header);
+  AIB_CUDA(cudaGetLastError());
+  build_fast_kernel<<<kFastSize / 256, 256, 0, s>>>(d_sym_lut, d_len_lut, max_bits, reinterpret_cast<uint2 *>(base),
+                                                    header);
+  AIB_CUDA(cudaGetLastError());
+  return AIB_OK;
+}
+
+AIB_API int aib_tables_flags(const void *d_tables, int32_t *flags_out, void *stream) {
+  if (!d_tables || !flags_out) return aib_set_error("aib_tables_flags: null pointer"), AIB_EINVAL;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  AIB_CUDA(cudaMemcpyAsync(&v, static_cast<const unsigned char *>(d_tables) + kFastBytes, 4, cudaMemcpyDeviceToHost, s));
+  AIB_CUDA(cudaStreamSynchronize(s));
+  *flags_out = v;
+  return AIB_OK;
+}
+
+AIB_API int aib_decode_bf16(const aib_stream_desc *desc, int32_t *d_status, void *stream) {
+  return launch<kModeBF16>(desc, 1, d_status, stream);
+}
+
+AIB_API int aib_decode_exponents_u8(const aib_stream_desc *desc, int32_t *d_status, void *stream) {
+  return launch<kModeU8>(desc, 1, d_status, stream);
+}
+
+AIB_API int aib_decode_exponents_i32(const aib_stream_desc *desc, int32_t *d_status, void *stream) {
+  return launch<kModeI32>(desc, 1, d_status, stream);
+}
+
+AIB_API int aib_decode_bf16_batch(const aib_stream_desc *descs, int count, int32_t *d_status, void *stream) {
+  return launch<kModeBF16>(descs, count, d_status, stream);
+}
+
+AIB_API int aib_recombine(const uint8_t *exponent, const uint8_t *sign_mantissa, int64_t n, uint16_t *out,
+                          void *stream) {
+  if (n < 0) return aib_set_error("aib_recombine: negative n"), AIB_EINVAL;
+  if (n == 0) return AIB_OK;
+  if (!exponent || !sign_mantissa || !out) return aib_set_error("aib_recombine: null pointer"), AIB_EINVAL;
+  if (!aligned(out, 2)) return aib_set_error("aib_recombine: out must be 2-byte aligned"), AIB_EINVAL;
+  DeviceInfo *di = nullptr;
+  int rc = device_info(&di);
+  if (rc != AIB_OK) return rc;
+  const int vec = aligned(exponent, 8) && aligned(sign_mantissa, 8) && aligned(out, 16);
+  const int64_t work = vec ? (n + 7) / 8 : n;
+  const int64_t blocks = std::min<int64_t>((work + 255) / 256, static_cast<int64_t>(di->sms) * 8);
+  recombine_kernel<<<static_cast<int>(std::max<int64_t>(blocks, 1)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      exponent, sign_mantissa, n, out, vec);
+  AIB_CUDA(cudaGetLastError());
+  return AIB_OK;
+}

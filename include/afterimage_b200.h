@@ -1,0 +1,147 @@
+/*
+ * afterimage_b200 -- C ABI of the B200 lossless BF16 weight-decode library
+ * (libafterimage_b200.so).
+ *
+ * The library replaces Afterimage's weight-reconstruction hot path: the
+ * chunked canonical-Huffman decode of BF16 exponent streams, merged with the
+ * raw (sign << 7) | mantissa bytes back into bit-identical BF16 weights.
+ * Every entry point takes plain pointers and sizes; device pointers are CUDA
+ * global-memory addresses on the current device, `stream` is a cudaStream_t
+ * (NULL = legacy default stream). Work is enqueued on `stream` and nothing
+ * synchronises unless the entry point says so. No entry point allocates
+ * device memory: callers own every buffer.
+ *
+ * Status: every function returns AIB_OK (0) or a nonzero AIB_E* code; the
+ * calling thread's message is available from aib_last_error().
+ *
+ * References are paths within the Afterimage project (afterimage-llm 0.3.0).
+ */
+#ifndef AFTERIMAGE_B200_H
+#define AFTERIMAGE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AIB_OK 0
+#define AIB_EINVAL 1 /* bad argument: caught on the host before any launch */
+#define AIB_ECUDA 2  /* a CUDA runtime call failed */
+
+/* Bits the decode kernels OR into the optional device status word. */
+#define AIB_STATUS_BAD_CHUNK_RANGE 1 /* a chunk's [offset, offset + nbytes) lies outside packed */
+#define AIB_STATUS_LUT_NOT_PREFIX 2  /* tables: LUT is not a prefix-code table; decoded exactly via the slow path */
+#define AIB_STATUS_LUT_RANGE 4       /* tables: a symbol outside [0, 255] or a length outside [0, max_bits] */
+#define AIB_STATUS_WAIT_TIMEOUT 8    /* a bounded wait on a bulk copy gave up; the CTA returned early */
+
+/* Thread-local message for the last failing call on this thread. */
+const char *aib_last_error(void);
+/* ABI version: bump on any signature change. */
+int aib_abi_version(void);
+
+/* ------------------------------------------------------------------------
+ * Encoder (host). Byte-identical to the reference encoder.
+ * ------------------------------------------------------------------------ */
+
+/* Field split of compress_layer (afterimage/runtime/compressed_store.py:78-88):
+ * exponent[i] = (bits >> 7) & 0xFF, sign_mantissa[i] = ((bits >> 15) & 1) << 7 | (bits & 0x7F). */
+int aib_split_bf16(const uint16_t *bits, int64_t n, uint8_t *exponent, uint8_t *sign_mantissa);
+/* np.bincount(symbols, minlength=256) (afterimage/runtime/huffman_chunked.py:159). */
+int aib_histogram(const uint8_t *symbols, int64_t n, int64_t counts[256]);
+/* build_lengths + canonical_codes (afterimage/runtime/huffman.py:41-125):
+ * natural Huffman depths (heapq tie-breaking), package-merge when deeper than
+ * max_bits_limit, canonical code assignment. *max_bits_out = longest code. */
+int aib_build_code(const int64_t counts[256], int max_bits_limit, int32_t lengths_out[256],
+                   uint32_t codes_out[256], int32_t *max_bits_out);
+/* build_decode_lut (afterimage/runtime/huffman.py:128-150): 2^max_bits entries. */
+int aib_build_decode_lut(const int32_t lengths[256], const uint32_t codes[256], int max_bits,
+                         int32_t *sym_lut, int8_t *len_lut);
+/* First packing pass (afterimage/runtime/huffman_chunked.py:41-78): bytes per chunk. */
+int aib_chunk_nbytes(const uint8_t *symbols, int64_t n, int64_t chunk_size,
+                     const int32_t lengths[256], int32_t *chunk_nbytes, int64_t *total_bytes);
+/* Second packing pass + offsets + 8-byte zero tail
+ * (afterimage/runtime/huffman_chunked.py:41-98, :178-201). */
+int aib_pack_chunks(const uint8_t *symbols, int64_t n, int64_t chunk_size,
+                    const int32_t lengths[256], const uint32_t codes[256],
+                    const int32_t *chunk_nbytes, int32_t *chunk_offsets, uint8_t *out,
+                    int64_t out_capacity);
+/* Host threads the encoder uses (OpenMP). */
+int aib_host_threads(void);
+
+/* ------------------------------------------------------------------------
+ * Decode tables -- replaces prepare_decode_tables
+ * (afterimage/runtime/gpu_decode_v2.py:71-76).
+ * ------------------------------------------------------------------------ */
+
+/* Size in bytes of one device table block (16-byte aligned buffer). */
+size_t aib_tables_bytes(void);
+/* Builds a tensor's table block from its reference LUTs, already on the
+ * device (sym_lut int32[2^max_bits], len_lut int8[2^max_bits]). The block
+ * holds a multi-symbol first-level table for shared memory plus validation
+ * flags; the decode kernels also read d_sym_lut / d_len_lut for codes longer
+ * than the first level, so those must stay alive while decoding.
+ * 0 <= max_bits <= 16. Stream-ordered; no synchronisation. */
+int aib_build_tables(const int32_t *d_sym_lut, const int8_t *d_len_lut, int max_bits,
+                     void *d_tables, void *stream);
+/* Copies the block's validation flags (AIB_STATUS_LUT_*) to *flags_out;
+ * synchronises `stream`. */
+int aib_tables_flags(const void *d_tables, int32_t *flags_out, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Decode. One descriptor names one tensor's compressed stream and the
+ * element range [elem_begin, elem_end) to produce.
+ * ------------------------------------------------------------------------ */
+typedef struct aib_stream_desc {
+  const uint8_t *packed;        /* device; 16-byte aligned; readable for packed_capacity bytes */
+  int64_t packed_capacity;      /* readable bytes at packed: multiple of 16, >= packed_nbytes */
+  int64_t packed_nbytes;        /* bytes of real stream data (chunk ranges are checked against it) */
+  int64_t offset_base;          /* chunk c starts at packed + chunk_offsets[c] - offset_base */
+  const int32_t *chunk_offsets; /* device; entry c - chunk_base is chunk c's byte offset */
+  const int32_t *chunk_nbytes;  /* device; entry c - chunk_base is chunk c's byte count */
+  int64_t chunk_base;           /* first chunk the two arrays above describe (0 = whole tensor) */
+  const void *tables;           /* device table block from aib_build_tables */
+  const int32_t *sym_lut;       /* device, int32[2^max_bits] */
+  const int8_t *len_lut;        /* device, int8[2^max_bits] */
+  int32_t max_bits;             /* 0..16, as stored with the tensor */
+  int32_t chunk_size;           /* symbols per chunk, >= 1 */
+  int64_t n_symbols;            /* symbols in the whole tensor */
+  int64_t elem_begin;           /* first element produced (0 <= elem_begin <= elem_end) */
+  int64_t elem_end;             /* one past the last element (<= n_symbols) */
+  const uint8_t *sign_mantissa; /* device; element elem_begin at index 0 (bf16 decode only) */
+  void *out;                    /* device; element elem_begin at index 0 */
+} aib_stream_desc;
+
+/* Fused decode + recombine: out (uint16 bf16 bits) = the reference's
+ * decompress output for elements [elem_begin, elem_end). Replaces the
+ * decode + _recombine pair of decompress_layer_gpu / decompress_rows_gpu
+ * (afterimage/runtime/compressed_store.py:186-240, :254-303, :94-114).
+ * d_status (optional, device int32) accumulates AIB_STATUS_* bits. */
+int aib_decode_bf16(const aib_stream_desc *desc, int32_t *d_status, void *stream);
+
+/* Exponent-only decode to uint8: replaces the _huffman_decode_kernel_v2
+ * launch of decode_gpu_v2 (afterimage/runtime/gpu_decode_v2.py:27-68, :107-114). */
+int aib_decode_exponents_u8(const aib_stream_desc *desc, int32_t *d_status, void *stream);
+
+/* Exponent-only decode to int32: replaces the _huffman_decode_kernel launch
+ * of decode_gpu (afterimage/runtime/gpu_decode.py:26-58, :61-75). */
+int aib_decode_exponents_i32(const aib_stream_desc *desc, int32_t *d_status, void *stream);
+
+/* Several tensors in one launch (a decoder layer's projections): replaces
+ * the per-tensor _decode_tensor loop of the layer streamer
+ * (afterimage/runtime/streaming_engine.py:1834-1842, :1074-1138).
+ * 1 <= count <= AIB_MAX_BATCH. */
+#define AIB_MAX_BATCH 16
+int aib_decode_bf16_batch(const aib_stream_desc *descs, int count, int32_t *d_status, void *stream);
+
+/* Elementwise recombine of an already-decoded exponent field: replaces
+ * recombine_exponent_and_sign_mantissa / _recombine
+ * (afterimage/runtime/compressed_store.py:94-130). */
+int aib_recombine(const uint8_t *exponent, const uint8_t *sign_mantissa, int64_t n, uint16_t *out,
+                  void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AFTERIMAGE_B200_H */

@@ -1,0 +1,99 @@
+"""The C-ABI library builds for sm_100a, loads on a CPU-only host and
+exports exactly the entry points include/afterimage_b200.h declares; host
+validation rejects bad arguments before any CUDA call."""
+import ctypes
+import pathlib
+import re
+
+import numpy as np
+import pytest
+
+from afterimage_b200 import _lib
+
+HEADER = pathlib.Path(__file__).resolve().parent.parent / "include" / "afterimage_b200.h"
+
+
+def declared_functions():
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    names = re.findall(r"^\s*(?:const\s+)?[a-z_0-9]+\s*\*?\s*(aib_[a-z_0-9]+)\s*\(", text, flags=re.M)
+    return sorted(set(names))
+
+
+def test_library_loads_and_exports_every_declared_symbol():
+    L = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 15, names
+    for n in names:
+        assert hasattr(L, n), f"{n} declared in the header but not exported"
+    assert sorted(n for n, _, _ in _lib.SIGNATURES) == names
+
+
+def test_library_exports_nothing_else():
+    import subprocess
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.lib_path())],
+                         capture_output=True, text=True, check=True).stdout
+    exported = sorted({line.split()[-1] for line in out.splitlines()
+                       if line.split()[1] in ("T", "W", "i")})
+    extra = [s for s in exported if not s.startswith("aib_") and not s.startswith("_init")
+             and not s.startswith("_fini")]
+    assert extra == [], extra[:20]
+
+
+def test_descriptor_layout_matches_header_order(tmp_path):
+    """ctypes' aib_stream_desc must have the C compiler's field offsets."""
+    import subprocess
+    fields = [f for f, _ in _lib.StreamDesc._fields_]
+    src = tmp_path / "layout.c"
+    src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"afterimage_b200.h\"\n"
+                   "int main(void){printf(\"%zu\\n\", sizeof(aib_stream_desc));"
+                   + "".join('printf("%%zu\\n", offsetof(aib_stream_desc, %s));' % f for f in fields)
+                   + "return 0;}\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    assert got[0] == ctypes.sizeof(_lib.StreamDesc)
+    assert got[1:] == [getattr(_lib.StreamDesc, f).offset for f in fields]
+
+
+def test_host_validation_rejects_bad_descriptors_without_a_gpu():
+    L = _lib.load()
+    d = _lib.StreamDesc()
+    d.chunk_size = 0
+    d.n_symbols = 10
+    d.elem_end = 10
+    rc = L.aib_decode_bf16(ctypes.byref(d), None, None)
+    assert rc == _lib.AIB_EINVAL
+    assert b"chunk_size" in L.aib_last_error()
+    d.chunk_size = 16
+    d.max_bits = 17
+    assert L.aib_decode_bf16(ctypes.byref(d), None, None) == _lib.AIB_EINVAL
+    assert b"max_bits" in L.aib_last_error()
+    d.max_bits = 8
+    d.elem_begin, d.elem_end = 5, 3
+    assert L.aib_decode_exponents_u8(ctypes.byref(d), None, None) == _lib.AIB_EINVAL
+    # empty range: nothing to do, no CUDA call needed
+    d.elem_begin, d.elem_end = 3, 3
+    assert L.aib_decode_exponents_u8(ctypes.byref(d), None, None) == _lib.AIB_OK
+    assert L.aib_decode_bf16_batch(ctypes.byref(d), 0, None, None) == _lib.AIB_EINVAL
+    assert L.aib_decode_bf16_batch(ctypes.byref(d), 17, None, None) == _lib.AIB_EINVAL
+
+
+def test_tables_bytes_and_abi_version():
+    L = _lib.load()
+    assert L.aib_abi_version() == 1
+    assert L.aib_tables_bytes() % 16 == 0 and L.aib_tables_bytes() >= 4096 * 8
+
+
+def test_encoder_entry_points_via_c_abi():
+    L = _lib.load()
+    bits = np.array([0, 0x8000, 0x7F80, 0xFF80, 0x3F80, 0xBF81, 1, 0x7F], dtype=np.uint16)
+    e = np.zeros(8, np.uint8)
+    sm = np.zeros(8, np.uint8)
+    assert L.aib_split_bf16(bits.ctypes.data, 8, e.ctypes.data, sm.ctypes.data) == 0
+    assert list(e) == [(int(b) >> 7) & 0xFF for b in bits]
+    assert list(sm) == [(((int(b) >> 15) & 1) << 7) | (int(b) & 0x7F) for b in bits]
+    counts = np.zeros(256, np.int64)
+    assert L.aib_histogram(e.ctypes.data, 8, counts.ctypes.data) == 0
+    assert counts.sum() == 8
+    assert L.aib_build_code(counts.ctypes.data, 0, None, None, None) == _lib.AIB_EINVAL
