@@ -143,24 +143,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
   return ok != 0;
 }
 
-__device__ __forceinline__ uint4 ld_blk(const uint4 *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
 __device__ __forceinline__ uint32_t bswap(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
-
-__device__ __forceinline__ uint2 slow_entry(uint64_t acc, const int32_t *__restrict__ sym_lut,
-                                            const int8_t *__restrict__ len_lut, int max_bits) {
-  // the reference LUT lookup itself: window = next max_bits bits
-  const uint32_t w = (static_cast<uint32_t>(acc >> 48)) >> (16 - max_bits);
-  const uint32_t s = static_cast<uint32_t>(__ldg(sym_lut + w)) & 0xFFu;
-  const uint32_t l = static_cast<uint32_t>(static_cast<int>(__ldg(len_lut + w))) & 0xFFu;
-  return make_uint2(s, 1u | (l << 8));
-}
 
 // 8 exponents + 8 sign/mantissa bytes -> 8 bf16 (bits = s<<15 | e<<7 | m).
 __device__ __forceinline__ uint4 combine8(uint2 ex, uint2 sm) {
@@ -199,6 +182,12 @@ __global__ void validate_lut_kernel(const int32_t *__restrict__ sym_lut, const i
   if (bad) atomicOr(flags, bad);
 }
 
+// Entry format of the first-level table (uint2 per 12-bit window):
+//   x = up to four decoded symbols, symbol i in byte i (unused bytes zero)
+//   y = bits consumed (bits 0..4) | 8 * symbol count (bits 8..15)
+// y == 0 marks a window whose first code is longer than 12 bits (or not
+// decidable from 12 bits): the kernel then looks the window up in the
+// reference LUT itself.
 __global__ void build_fast_kernel(const int32_t *__restrict__ sym_lut, const int8_t *__restrict__ len_lut,
                                   int max_bits, uint2 *fast, int32_t *header) {
   const int v = blockIdx.x * blockDim.x + threadIdx.x;
@@ -229,12 +218,69 @@ __global__ void build_fast_kernel(const int32_t *__restrict__ sym_lut, const int
     ++cnt;
     p += l;
   }
-  fast[v] = make_uint2(syms, static_cast<uint32_t>(cnt) | (static_cast<uint32_t>(p) << 8));
+  fast[v] = cnt == 0 ? make_uint2(0u, 0u)
+                     : make_uint2(syms, static_cast<uint32_t>(p) | (static_cast<uint32_t>(8 * cnt) << 8));
 }
 
 // ---------------------------------------------------------------------------
 // the decode kernel
 // ---------------------------------------------------------------------------
+// Per-lane bit reader over one chunk: a 64-bit MSB-aligned buffer `acc`
+// holding `nb` valid bits, fed 32 bits at a time from a queue of big-endian
+// words (q0..q3, `qn` left) that is refilled from 16-byte aligned loads
+// issued two blocks ahead (pa, pb).
+struct Reader {
+  uint64_t acc;
+  int nb;
+  uint32_t q0, q1, q2, q3;
+  int qn;
+  uint4 pa, pb;
+  int64_t bi;  // next 16-byte block to load
+};
+
+__device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::evict_last.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ void reader_next_block(Reader &r, const uint4 *src, int64_t bmax) {
+  r.q0 = bswap(r.pa.x); r.q1 = bswap(r.pa.y); r.q2 = bswap(r.pa.z); r.q3 = bswap(r.pa.w);
+  r.qn = 4;
+  r.pa = r.pb;
+  r.pb = ld_stream(src + min(r.bi, bmax));
+  ++r.bi;
+}
+
+__device__ __forceinline__ void reader_refill(Reader &r, const uint4 *src, int64_t bmax) {
+  r.acc |= static_cast<uint64_t>(r.q0) << (32 - r.nb);
+  r.nb += 32;
+  r.q0 = r.q1; r.q1 = r.q2; r.q2 = r.q3;
+  if (--r.qn == 0) reader_next_block(r, src, bmax);
+}
+
+__device__ __forceinline__ void reader_init(Reader &r, const uint4 *src, int64_t bmax, int64_t pos) {
+  r.bi = pos >> 4;
+  const uint4 b0 = ld_stream(src + min(r.bi, bmax));
+  r.pa = ld_stream(src + min(r.bi + 1, bmax));
+  r.pb = ld_stream(src + min(r.bi + 2, bmax));
+  r.bi += 3;
+  uint32_t w0 = bswap(b0.x), w1 = bswap(b0.y), w2 = bswap(b0.z), w3 = bswap(b0.w);
+  const int wofs = static_cast<int>((pos >> 2) & 3);
+  if (wofs & 2) { uint32_t t0 = w0, t1 = w1; w0 = w2; w1 = w3; w2 = t0; w3 = t1; }
+  if (wofs & 1) { uint32_t t0 = w0; w0 = w1; w1 = w2; w2 = w3; w3 = t0; }
+  r.q0 = w0; r.q1 = w1; r.q2 = w2; r.q3 = w3;
+  r.qn = 4 - wofs;
+  r.acc = 0;
+  r.nb = 0;
+  reader_refill(r, src, bmax);  // first word, then drop the bytes before the chunk start
+  const int skip = static_cast<int>(pos & 3) * 8;
+  r.acc <<= skip;
+  r.nb -= skip;
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ Batch batch,
                                                           int32_t *status) {
@@ -255,20 +301,26 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   __syncthreads();
   {
     unsigned spins = 0;
-    bool timed_out = false;
+    int timed_out = 0;
     while (!mbar_try_wait(&bar, 0)) {
       if (++spins > kWaitLimit) {
-        timed_out = true;
+        timed_out = 1;
         break;
       }
       __nanosleep(64);
     }
-    if (timed_out) {
-      if (status) atomicOr(status, AIB_STATUS_WAIT_TIMEOUT);
+    // the whole CTA leaves together so no barrier below misses a thread
+    if (__syncthreads_or(timed_out)) {
+      if (status && threadIdx.x == 0) atomicOr(status, AIB_STATUS_WAIT_TIMEOUT);
       return;
     }
   }
-  const bool force_slow = (*J.flags) != 0;
+  if (*J.flags != 0) {
+    // not a prefix-code LUT (or out-of-range entries): route every lookup
+    // through the reference LUT itself
+    for (int i = threadIdx.x; i < kFastSize; i += kThreads) s_fast[i] = make_uint2(0u, 0u);
+    __syncthreads();
+  }
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -278,21 +330,24 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   const int max_bits = J.max_bits;
   const uint4 *src = reinterpret_cast<const uint4 *>(J.packed);
   const int64_t bmax = J.packed_cap / 16 - 1;
+  // lane's slot in the fast merge: chunk (lane >> 3) + 4 * it, 8 symbols at (lane & 7) * 8
+  const int64_t lane_elem = (lane >> 3) * cs + (lane & 7) * 8;
+  const int64_t it_stride = 4 * cs;
+  const int ring_rd = (lane >> 3) * kRow + (lane & 7) * 8;
 
   for (int64_t grp = static_cast<int64_t>(blockIdx.x - J.cta_begin) * kWarps + warp; grp < J.n_groups;
        grp += static_cast<int64_t>(J.ctas) * kWarps) {
     const int64_t c0 = J.c_begin + grp * 32;
     const int64_t c = c0 + lane;
     const bool active = c < J.c_end;
-    const int64_t chunk_e0 = c * cs;
-    const int need = active ? static_cast<int>(min(cs, J.e1 - chunk_e0)) : 0;
+    const int64_t ge0 = c0 * cs;  // first element of the group
+    // warp-uniform: all 32 chunks complete and inside [e0, e1), phases whole
+    const bool fast = J.vec_ok && (cs % kPhase) == 0 && ge0 >= J.e0 && ge0 + 32 * cs <= J.e1;
+    const int need = active ? static_cast<int>(min(cs, J.e1 - c * cs)) : 0;
 
-    // ---- bit reader set-up -------------------------------------------------
-    uint64_t acc = 0;
-    int nb = 0;
-    uint4 q = make_uint4(0, 0, 0, 0), nxt = make_uint4(0, 0, 0, 0);
-    int qn = 4;
-    int64_t bi = 0;
+    Reader rd;
+    rd.acc = 0; rd.nb = 0; rd.q0 = rd.q1 = rd.q2 = rd.q3 = 0; rd.qn = 4; rd.bi = 0;
+    rd.pa = make_uint4(0, 0, 0, 0); rd.pb = rd.pa;
     if (active) {
       int64_t pos = static_cast<int64_t>(J.offs[c - J.chunk_base]) - J.offset_base;
       const int64_t nbyt = J.nbytes[c - J.chunk_base];
@@ -300,90 +355,67 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         if (status) atomicOr(status, AIB_STATUS_BAD_CHUNK_RANGE);
         pos = 0;
       }
-      bi = pos >> 4;
-      const uint4 b0 = ld_blk(src + min(bi, bmax));
-      nxt = ld_blk(src + min(bi + 1, bmax));
-      bi += 2;
-      q = make_uint4(bswap(b0.x), bswap(b0.y), bswap(b0.z), bswap(b0.w));
-      const int wofs = static_cast<int>((pos >> 2) & 3);
-      if (wofs & 2) q = make_uint4(q.z, q.w, q.x, q.y);
-      if (wofs & 1) q = make_uint4(q.y, q.z, q.w, q.x);
-      qn = 4 - wofs;
-      // first word, then drop the bytes before the chunk start
-      acc = static_cast<uint64_t>(q.x) << 32;
-      nb = 32;
-      q.x = q.y; q.y = q.z; q.z = q.w;
-      if (--qn == 0) {
-        q = make_uint4(bswap(nxt.x), bswap(nxt.y), bswap(nxt.z), bswap(nxt.w));
-        qn = 4;
-        nxt = ld_blk(src + min(bi, bmax));
-        ++bi;
-      }
-      const int skip = static_cast<int>(pos & 3) * 8;
-      acc <<= skip;
-      nb -= skip;
+      reader_init(rd, src, bmax, pos);
     }
 
-    const int max_need = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(need));
-    int k = 0;     // symbols flushed to the ring (multiple of 4)
-    int nout = 0;  // symbols pending in outacc
-    uint64_t outacc = 0;
+    const int max_need = fast ? static_cast<int>(cs)
+                              : static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(need)));
+    int k = 0;              // symbols flushed to the ring (multiple of 4)
+    int n8 = 0;             // 8 x symbols pending in olo:ohi
+    uint32_t olo = 0, ohi = 0;
+    const int64_t grp_out = ge0 - J.e0;  // output index of the group's first element (fast path)
 
     for (int ph = 0; ph < max_need; ph += kPhase) {
+      uint2 smv[8];
+      if (MODE == kModeBF16 && fast) {
+        // issue this phase's sign/mantissa loads now; they land while the
+        // lanes decode
+        const uint8_t *smp = J.sm + grp_out + lane_elem + ph;
+#pragma unroll
+        for (int it = 0; it < 8; ++it) smv[it] = __ldcs(reinterpret_cast<const uint2 *>(smp + it * it_stride));
+      }
       const int target = min(ph + kPhase, need);
-      while (k + nout < target) {
-        if (nb < 32) {
-          acc |= static_cast<uint64_t>(q.x) << (32 - nb);
-          nb += 32;
-          q.x = q.y; q.y = q.z; q.z = q.w;
-          if (--qn == 0) {
-            q = make_uint4(bswap(nxt.x), bswap(nxt.y), bswap(nxt.z), bswap(nxt.w));
-            qn = 4;
-            nxt = ld_blk(src + min(bi, bmax));
-            ++bi;
-          }
-        }
+      while (k + (n8 >> 3) < target) {
+        if (rd.nb < 32) reader_refill(rd, src, bmax);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
-          uint2 e = s_fast[static_cast<uint32_t>(acc >> (64 - kFastBits))];
-          if (force_slow || (e.y & 7u) == 0u) e = slow_entry(acc, J.sym_lut, J.len_lut, max_bits);
-          const uint32_t used = e.y >> 8;
-          acc <<= used;
-          nb -= static_cast<int>(used);
-          outacc |= static_cast<uint64_t>(e.x) << (8 * nout);
-          nout += static_cast<int>(e.y & 7u);
-          if (nout >= 4) {
-            *reinterpret_cast<uint32_t *>(my_ring + (k & (kRing - 1))) = static_cast<uint32_t>(outacc);
-            outacc >>= 32;
-            nout -= 4;
+          uint2 e = s_fast[static_cast<uint32_t>(rd.acc >> (64 - kFastBits))];
+          if (e.y == 0u) {
+            // code longer than the first level: the reference LUT lookup
+            const uint32_t w = (static_cast<uint32_t>(rd.acc >> 48)) >> (16 - max_bits);
+            const uint32_t s = static_cast<uint32_t>(__ldg(J.sym_lut + w)) & 0xFFu;
+            const uint32_t l = static_cast<uint32_t>(static_cast<int>(__ldg(J.len_lut + w))) & 31u;
+            e = make_uint2(s, l | (8u << 8));
+          }
+          const uint32_t used = e.y & 31u;
+          rd.acc <<= used;
+          rd.nb -= static_cast<int>(used);
+          olo |= e.x << n8;
+          ohi |= __funnelshift_l(e.x, 0u, static_cast<uint32_t>(n8));
+          n8 += static_cast<int>(e.y >> 8);
+          if (n8 >= 32) {
+            *reinterpret_cast<uint32_t *>(my_ring + (k & (kRing - 1))) = olo;
+            olo = ohi;
+            ohi = 0;
+            n8 -= 32;
             k += 4;
           }
         }
       }
       if (k < target)  // end of this lane's range: flush the partial word
-        *reinterpret_cast<uint32_t *>(my_ring + (k & (kRing - 1))) = static_cast<uint32_t>(outacc);
+        *reinterpret_cast<uint32_t *>(my_ring + (k & (kRing - 1))) = olo;
       __syncwarp();
 
-      // ---- merge: 32 chunks x kPhase symbols, 8 elements per lane-step ------
-#pragma unroll 2
-      for (int it = 0; it < kPhase * 32 / 8 / 32; ++it) {
-        const int r = it * 4 + (lane >> 3);
-        const int q8 = (lane & 7) * 8;
-        const int64_t cr = c0 + r;
-        if (cr >= J.c_end) continue;
-        const int64_t base = cr * cs;
-        const int64_t lo = max(base, J.e0);
-        const int64_t hi = min(base + cs, J.e1);
-        const int64_t g = base + ph + q8;
-        if (g >= hi || g + 8 <= lo) continue;
-        const unsigned char *rrow = ring_base + r * kRow;
-        const int ro = (ph + q8) & (kRing - 1);
-        const int64_t oi = g - J.e0;
-        if (J.vec_ok && g >= lo && g + 8 <= hi) {
-          const uint2 ex = *reinterpret_cast<const uint2 *>(rrow + ro);
+      if (fast) {
+        // ---- merge, interior group: 32 chunks x kPhase symbols, 16-byte stores
+        const unsigned char *rr = ring_base + ring_rd + (ph & (kRing - 1));
+        const int64_t ob = grp_out + lane_elem + ph;
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const uint2 ex = *reinterpret_cast<const uint2 *>(rr + it * 4 * kRow);
+          const int64_t oi = ob + it * it_stride;
           if (MODE == kModeBF16) {
-            const uint2 smv = __ldcs(reinterpret_cast<const uint2 *>(J.sm + oi));
-            __stcs(reinterpret_cast<uint4 *>(static_cast<uint16_t *>(J.out) + oi), combine8(ex, smv));
+            __stcs(reinterpret_cast<uint4 *>(static_cast<uint16_t *>(J.out) + oi), combine8(ex, smv[it]));
           } else if (MODE == kModeU8) {
             __stcs(reinterpret_cast<uint2 *>(static_cast<uint8_t *>(J.out) + oi), ex);
           } else {
@@ -396,18 +428,46 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
             __stcs(reinterpret_cast<uint4 *>(o), a);
             __stcs(reinterpret_cast<uint4 *>(o + 4), b);
           }
-        } else {
-          for (int jj = 0; jj < 8; ++jj) {
-            const int64_t gg = g + jj;
-            if (gg < lo || gg >= hi) continue;
-            const uint32_t e = rrow[(ro + jj) & (kRing - 1)];
-            const int64_t o = gg - J.e0;
-            if (MODE == kModeBF16)
-              static_cast<uint16_t *>(J.out)[o] = combine1(e, J.sm[o]);
-            else if (MODE == kModeU8)
-              static_cast<uint8_t *>(J.out)[o] = static_cast<uint8_t>(e);
-            else
-              static_cast<int32_t *>(J.out)[o] = static_cast<int32_t>(e);
+        }
+      } else {
+        // ---- merge, general group: ragged ranges, odd chunk sizes, edges
+        for (int it = 0; it < kPhase * 32 / 8 / 32; ++it) {
+          const int r = it * 4 + (lane >> 3);
+          const int q8 = (lane & 7) * 8;
+          const int64_t cr = c0 + r;
+          if (cr >= J.c_end) continue;
+          const int64_t base = cr * cs;
+          const int64_t lo = max(base, J.e0);
+          const int64_t hi = min(base + cs, J.e1);
+          const int64_t g = base + ph + q8;
+          if (g >= hi || g + 8 <= lo) continue;
+          const unsigned char *rrow = ring_base + r * kRow;
+          const int ro = (ph + q8) & (kRing - 1);
+          const int64_t oi = g - J.e0;
+          if (J.vec_ok && g >= lo && g + 8 <= hi) {
+            const uint2 ex = *reinterpret_cast<const uint2 *>(rrow + ro);
+            if (MODE == kModeBF16) {
+              const uint2 s8 = __ldcs(reinterpret_cast<const uint2 *>(J.sm + oi));
+              __stcs(reinterpret_cast<uint4 *>(static_cast<uint16_t *>(J.out) + oi), combine8(ex, s8));
+            } else if (MODE == kModeU8) {
+              __stcs(reinterpret_cast<uint2 *>(static_cast<uint8_t *>(J.out) + oi), ex);
+            } else {
+              int32_t *o = static_cast<int32_t *>(J.out) + oi;
+              for (int jj = 0; jj < 8; ++jj) o[jj] = static_cast<int32_t>(rrow[ro + jj]);
+            }
+          } else {
+            for (int jj = 0; jj < 8; ++jj) {
+              const int64_t gg = g + jj;
+              if (gg < lo || gg >= hi) continue;
+              const uint32_t e = rrow[(ro + jj) & (kRing - 1)];
+              const int64_t o = gg - J.e0;
+              if (MODE == kModeBF16)
+                static_cast<uint16_t *>(J.out)[o] = combine1(e, J.sm[o]);
+              else if (MODE == kModeU8)
+                static_cast<uint8_t *>(J.out)[o] = static_cast<uint8_t>(e);
+              else
+                static_cast<int32_t *>(J.out)[o] = static_cast<int32_t>(e);
+            }
           }
         }
       }
@@ -547,7 +607,7 @@ static int make_job(const aib_stream_desc *d, int mode, Job *j, bool *empty) {
 }
 
 // groups of 32 chunks handled per warp before a CTA is considered full
-static constexpr int kGroupsPerWarp = 2;
+static constexpr int kGroupsPerWarp = 1;
 
 template <int MODE>
 static int launch(const aib_stream_desc *descs, int count, int32_t *status, void *stream) {
