@@ -61,17 +61,33 @@ void aib_set_errorf(const char *fmt, ...) {
 
 namespace aib {
 
+// Tuning parameters (compile-time; -D overrides exist for sweeps).
+#ifndef AIB_WARPS
+#define AIB_WARPS 8
+#endif
+#ifndef AIB_PHASE
+#define AIB_PHASE 64
+#endif
+#ifndef AIB_MIN_BLOCKS
+#define AIB_MIN_BLOCKS 2
+#endif
+#ifndef AIB_SLOTS
+#define AIB_SLOTS 4
+#endif
 constexpr int kFastBits = 12;
 constexpr int kFastSize = 1 << kFastBits;
 constexpr int kFastBytes = kFastSize * 8;
 constexpr int kTablesBytes = kFastBytes + 16;  // fast table + {flags, max_bits, pad}
-constexpr int kWarps = 8;
+constexpr int kWarps = AIB_WARPS;
 constexpr int kThreads = kWarps * 32;
-constexpr int kPhase = 64;        // symbols per lane between merges
-constexpr int kRing = 128;        // ring bytes per lane (power of two >= kPhase + 11)
+constexpr int kPhase = AIB_PHASE;  // symbols per lane between merges (multiple of 32)
+constexpr int kRing = kPhase * 2;  // ring bytes per lane (power of two >= kPhase + 11)
 constexpr int kRow = kRing + 8;   // padded row: lanes at equal k hit different banks
 constexpr int kRingWarpBytes = 32 * kRow;
-constexpr int kSmemBytes = kFastBytes + kWarps * kRingWarpBytes;
+constexpr int kSlots = AIB_SLOTS;                // stream ring slots per lane (power of two >= 2)
+constexpr int kSlotRow = kSlots * 16 + 16;       // padded: lanes' slot k spread over the banks
+constexpr int kStreamWarpBytes = 32 * kSlotRow;
+constexpr int kSmemBytes = kFastBytes + kWarps * (kRingWarpBytes + kStreamWarpBytes);
 constexpr unsigned kWaitLimit = 1u << 22;  // bounded mbarrier wait (~0.3 s with backoff)
 
 enum Mode { kModeBF16 = 0, kModeU8 = 1, kModeI32 = 2 };
@@ -225,57 +241,108 @@ __global__ void build_fast_kernel(const int32_t *__restrict__ sym_lut, const int
 // ---------------------------------------------------------------------------
 // the decode kernel
 // ---------------------------------------------------------------------------
+// L2 policies: a chunk's compressed bytes are fetched 16 bytes at a time
+// over its whole decode, so they are kept (evict_last) and fetched 256 bytes
+// at a time; sign/mantissa bytes and BF16 output are touched once and leave
+// L2 first.
+__device__ __forceinline__ uint64_t policy_keep() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint64_t policy_stream() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+__device__ __forceinline__ uint2 ld_once8(const void *p, uint64_t pol) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v2.u32 {%0,%1}, [%2], %3;"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p), "l"(pol));
+  return v;
+}
+
+__device__ __forceinline__ void st_once16(void *p, uint4 v, uint64_t pol) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.v4.u32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(p), "r"(v.x),
+               "r"(v.y), "r"(v.z), "r"(v.w), "l"(pol)
+               : "memory");
+}
+
+__device__ __forceinline__ void st_once8(void *p, uint2 v, uint64_t pol) {
+  asm volatile("st.global.L1::no_allocate.L2::cache_hint.v2.u32 [%0], {%1,%2}, %3;" ::"l"(p), "r"(v.x), "r"(v.y),
+               "l"(pol)
+               : "memory");
+}
+
+__device__ __forceinline__ void prefetch_l2(const void *p) { asm volatile("prefetch.global.L2 [%0];" ::"l"(p)); }
+
+// 16-byte asynchronous global -> shared copy (no register involvement); each
+// copy is its own commit group so a lane can wait for its oldest block only.
+__device__ __forceinline__ void cp_async16(void *sdst, const void *gsrc, uint64_t pol) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint.L2::256B [%0], [%1], 16, 16, %2;\n"
+               "cp.async.commit_group;" ::"r"(smem_u32(sdst)),
+               "l"(gsrc), "l"(pol)
+               : "memory");
+}
+
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
 // Per-lane bit reader over one chunk: a 64-bit MSB-aligned buffer `acc`
-// holding `nb` valid bits, fed 32 bits at a time from a queue of big-endian
-// words (q0..q3, `qn` left) that is refilled from 16-byte aligned loads
-// issued two blocks ahead (pa, pb).
+// holding `nb` valid bits, fed 32 bits at a time from the current 16-byte
+// block (big-endian words q0..q3, `qn` left). Blocks stream through a
+// per-lane shared-memory ring of kSlots 16-byte slots: kSlots - 1 copies are
+// always in flight, so a block is requested ~(kSlots - 1) * 16 bytes before
+// the lane reaches it.
 struct Reader {
   uint64_t acc;
   int nb;
   uint32_t q0, q1, q2, q3;
   int qn;
-  uint4 pa, pb;
-  int64_t bi;  // next 16-byte block to load
+  int slot;    // slot holding the next block to consume
+  int64_t bi;  // next 16-byte block to request
 };
 
-__device__ __forceinline__ uint4 ld_stream(const uint4 *p) {
-  uint4 v;
-  asm volatile("ld.global.nc.L1::evict_last.v4.u32 {%0,%1,%2,%3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "l"(p));
-  return v;
-}
-
-__device__ __forceinline__ void reader_next_block(Reader &r, const uint4 *src, int64_t bmax) {
-  r.q0 = bswap(r.pa.x); r.q1 = bswap(r.pa.y); r.q2 = bswap(r.pa.z); r.q3 = bswap(r.pa.w);
+__device__ __forceinline__ void reader_next_block(Reader &r, unsigned char *ring, const uint4 *src, int64_t bmax,
+                                                  uint64_t pol) {
+  cp_async_wait<kSlots - 2>();  // the oldest outstanding copy is the block needed now
+  const uint4 b = *reinterpret_cast<const uint4 *>(ring + r.slot * 16);
+  r.q0 = bswap(b.x); r.q1 = bswap(b.y); r.q2 = bswap(b.z); r.q3 = bswap(b.w);
   r.qn = 4;
-  r.pa = r.pb;
-  r.pb = ld_stream(src + min(r.bi, bmax));
+  // block bi belongs in the slot drained by the previous call: slot (slot - 1)
+  cp_async16(ring + ((r.slot + kSlots - 1) & (kSlots - 1)) * 16, src + min(r.bi, bmax), pol);
   ++r.bi;
+  r.slot = (r.slot + 1) & (kSlots - 1);
 }
 
-__device__ __forceinline__ void reader_refill(Reader &r, const uint4 *src, int64_t bmax) {
+__device__ __forceinline__ void reader_refill(Reader &r, unsigned char *ring, const uint4 *src, int64_t bmax,
+                                              uint64_t pol) {
   r.acc |= static_cast<uint64_t>(r.q0) << (32 - r.nb);
   r.nb += 32;
   r.q0 = r.q1; r.q1 = r.q2; r.q2 = r.q3;
-  if (--r.qn == 0) reader_next_block(r, src, bmax);
+  if (--r.qn == 0) reader_next_block(r, ring, src, bmax, pol);
 }
 
-__device__ __forceinline__ void reader_init(Reader &r, const uint4 *src, int64_t bmax, int64_t pos) {
-  r.bi = pos >> 4;
-  const uint4 b0 = ld_stream(src + min(r.bi, bmax));
-  r.pa = ld_stream(src + min(r.bi + 1, bmax));
-  r.pb = ld_stream(src + min(r.bi + 2, bmax));
-  r.bi += 3;
-  uint32_t w0 = bswap(b0.x), w1 = bswap(b0.y), w2 = bswap(b0.z), w3 = bswap(b0.w);
+__device__ __forceinline__ void reader_init(Reader &r, unsigned char *ring, const uint4 *src, int64_t bmax,
+                                            int64_t pos, uint64_t pol) {
+  const int64_t b0 = pos >> 4;
+#pragma unroll
+  for (int s = 0; s < kSlots - 1; ++s) cp_async16(ring + s * 16, src + min(b0 + s, bmax), pol);
+  r.bi = b0 + kSlots - 1;
+  r.slot = 0;
+  reader_next_block(r, ring, src, bmax, pol);  // block b0 into q, request b0 + kSlots - 1
   const int wofs = static_cast<int>((pos >> 2) & 3);
-  if (wofs & 2) { uint32_t t0 = w0, t1 = w1; w0 = w2; w1 = w3; w2 = t0; w3 = t1; }
-  if (wofs & 1) { uint32_t t0 = w0; w0 = w1; w1 = w2; w2 = w3; w3 = t0; }
-  r.q0 = w0; r.q1 = w1; r.q2 = w2; r.q3 = w3;
+  if (wofs & 2) { uint32_t t0 = r.q0, t1 = r.q1; r.q0 = r.q2; r.q1 = r.q3; r.q2 = t0; r.q3 = t1; }
+  if (wofs & 1) { uint32_t t0 = r.q0; r.q0 = r.q1; r.q1 = r.q2; r.q2 = r.q3; r.q3 = t0; }
   r.qn = 4 - wofs;
   r.acc = 0;
   r.nb = 0;
-  reader_refill(r, src, bmax);  // first word, then drop the bytes before the chunk start
+  reader_refill(r, ring, src, bmax, pol);  // first word, then drop the bytes before the chunk start
   const int skip = static_cast<int>(pos & 3) * 8;
   r.acc <<= skip;
   r.nb -= skip;
@@ -326,14 +393,21 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   const int lane = threadIdx.x & 31;
   unsigned char *ring_base = smem + kFastBytes + warp * kRingWarpBytes;
   unsigned char *my_ring = ring_base + lane * kRow;
+  unsigned char *my_stream = smem + kFastBytes + kWarps * kRingWarpBytes + warp * kStreamWarpBytes + lane * kSlotRow;
   const int64_t cs = J.chunk_size;
   const int max_bits = J.max_bits;
   const uint4 *src = reinterpret_cast<const uint4 *>(J.packed);
   const int64_t bmax = J.packed_cap / 16 - 1;
-  // lane's slot in the fast merge: chunk (lane >> 3) + 4 * it, 8 symbols at (lane & 7) * 8
-  const int64_t lane_elem = (lane >> 3) * cs + (lane & 7) * 8;
-  const int64_t it_stride = 4 * cs;
-  const int ring_rd = (lane >> 3) * kRow + (lane & 7) * 8;
+  // lane's slot in the merge: each chunk's kPhase symbols are kVecs 8-symbol
+  // vectors; lane covers vector (lane % kVecs) of chunk (lane / kVecs) + kRowsPerIt * it
+  constexpr int kVecs = kPhase / 8;
+  constexpr int kRowsPerIt = 32 / kVecs;
+  constexpr int kIters = kPhase * 32 / 8 / 32;
+  const int64_t lane_elem = (lane / kVecs) * cs + (lane % kVecs) * 8;
+  const int64_t it_stride = kRowsPerIt * cs;
+  const int ring_rd = (lane / kVecs) * kRow + (lane % kVecs) * 8;
+  const uint64_t pol_keep = policy_keep();
+  const uint64_t pol_once = policy_stream();
 
   for (int64_t grp = static_cast<int64_t>(blockIdx.x - J.cta_begin) * kWarps + warp; grp < J.n_groups;
        grp += static_cast<int64_t>(J.ctas) * kWarps) {
@@ -347,7 +421,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
 
     Reader rd;
     rd.acc = 0; rd.nb = 0; rd.q0 = rd.q1 = rd.q2 = rd.q3 = 0; rd.qn = 4; rd.bi = 0;
-    rd.pa = make_uint4(0, 0, 0, 0); rd.pb = rd.pa;
+    rd.slot = 0;
     if (active) {
       int64_t pos = static_cast<int64_t>(J.offs[c - J.chunk_base]) - J.offset_base;
       const int64_t nbyt = J.nbytes[c - J.chunk_base];
@@ -355,7 +429,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         if (status) atomicOr(status, AIB_STATUS_BAD_CHUNK_RANGE);
         pos = 0;
       }
-      reader_init(rd, src, bmax, pos);
+      reader_init(rd, my_stream, src, bmax, pos, pol_keep);
     }
 
     const int max_need = fast ? static_cast<int>(cs)
@@ -366,17 +440,19 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     const int64_t grp_out = ge0 - J.e0;  // output index of the group's first element (fast path)
 
     for (int ph = 0; ph < max_need; ph += kPhase) {
-      uint2 smv[8];
+      uint2 smv[kIters];
       if (MODE == kModeBF16 && fast) {
         // issue this phase's sign/mantissa loads now; they land while the
         // lanes decode
         const uint8_t *smp = J.sm + grp_out + lane_elem + ph;
 #pragma unroll
-        for (int it = 0; it < 8; ++it) smv[it] = __ldcs(reinterpret_cast<const uint2 *>(smp + it * it_stride));
+        for (int it = 0; it < kIters; ++it) smv[it] = ld_once8(smp + it * it_stride, pol_once);
+        // warm L2 with this lane's chunk segment of the next phase
+        if (ph + kPhase < max_need) prefetch_l2(J.sm + grp_out + static_cast<int64_t>(lane) * cs + ph + kPhase);
       }
       const int target = min(ph + kPhase, need);
       while (k + (n8 >> 3) < target) {
-        if (rd.nb < 32) reader_refill(rd, src, bmax);
+        if (rd.nb < 32) reader_refill(rd, my_stream, src, bmax, pol_keep);
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           uint2 e = s_fast[static_cast<uint32_t>(rd.acc >> (64 - kFastBits))];
@@ -411,13 +487,13 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         const unsigned char *rr = ring_base + ring_rd + (ph & (kRing - 1));
         const int64_t ob = grp_out + lane_elem + ph;
 #pragma unroll
-        for (int it = 0; it < 8; ++it) {
-          const uint2 ex = *reinterpret_cast<const uint2 *>(rr + it * 4 * kRow);
+        for (int it = 0; it < kIters; ++it) {
+          const uint2 ex = *reinterpret_cast<const uint2 *>(rr + it * kRowsPerIt * kRow);
           const int64_t oi = ob + it * it_stride;
           if (MODE == kModeBF16) {
-            __stcs(reinterpret_cast<uint4 *>(static_cast<uint16_t *>(J.out) + oi), combine8(ex, smv[it]));
+            st_once16(static_cast<uint16_t *>(J.out) + oi, combine8(ex, smv[it]), pol_once);
           } else if (MODE == kModeU8) {
-            __stcs(reinterpret_cast<uint2 *>(static_cast<uint8_t *>(J.out) + oi), ex);
+            st_once8(static_cast<uint8_t *>(J.out) + oi, ex, pol_once);
           } else {
             uint4 a, b;
             a.x = __byte_perm(ex.x, 0, 0x4440); a.y = __byte_perm(ex.x, 0, 0x4441);
@@ -431,9 +507,9 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         }
       } else {
         // ---- merge, general group: ragged ranges, odd chunk sizes, edges
-        for (int it = 0; it < kPhase * 32 / 8 / 32; ++it) {
-          const int r = it * 4 + (lane >> 3);
-          const int q8 = (lane & 7) * 8;
+        for (int it = 0; it < kIters; ++it) {
+          const int r = it * kRowsPerIt + lane / kVecs;
+          const int q8 = (lane % kVecs) * 8;
           const int64_t cr = c0 + r;
           if (cr >= J.c_end) continue;
           const int64_t base = cr * cs;
@@ -473,6 +549,9 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
       }
       __syncwarp();
     }
+    // drain this lane's stream copies before its slots are reused (or the
+    // kernel exits)
+    cp_async_wait<0>();
   }
 }
 
