@@ -63,18 +63,24 @@ namespace aib {
 
 // Tuning parameters (compile-time; -D overrides exist for sweeps).
 #ifndef AIB_WARPS
-#define AIB_WARPS 8
+#define AIB_WARPS 24
 #endif
 #ifndef AIB_PHASE
 #define AIB_PHASE 64
 #endif
 #ifndef AIB_MIN_BLOCKS
-#define AIB_MIN_BLOCKS 2
+#define AIB_MIN_BLOCKS 1
 #endif
 #ifndef AIB_SLOTS
 #define AIB_SLOTS 4
 #endif
-constexpr int kFastBits = 12;
+#ifndef AIB_FAST_BITS
+#define AIB_FAST_BITS 12
+#endif
+#ifndef AIB_AHEAD
+#define AIB_AHEAD 1
+#endif
+constexpr int kFastBits = AIB_FAST_BITS;
 constexpr int kFastSize = 1 << kFastBits;
 constexpr int kFastBytes = kFastSize * 8;
 constexpr int kTablesBytes = kFastBytes + 16;  // fast table + {flags, max_bits, pad}
@@ -91,6 +97,7 @@ constexpr int kSmemBytes = kFastBytes + kWarps * (kRingWarpBytes + kStreamWarpBy
 constexpr unsigned kWaitLimit = 1u << 22;  // bounded mbarrier wait (~0.3 s with backoff)
 
 enum Mode { kModeBF16 = 0, kModeU8 = 1, kModeI32 = 2 };
+constexpr int kDefaultChunk = 1024;  // compress_layer's default chunk_size
 
 struct Job {
   const uint8_t *packed;
@@ -165,10 +172,11 @@ __device__ __forceinline__ uint32_t bswap(uint32_t x) { return __byte_perm(x, 0,
 __device__ __forceinline__ uint4 combine8(uint2 ex, uint2 sm) {
   const uint32_t M = 0x807F807Fu;
   uint4 o;
-  o.x = (__byte_perm(ex.x, 0, 0x4140) << 7) | (__byte_perm(sm.x, 0, 0x1100) & M);
-  o.y = (__byte_perm(ex.x, 0, 0x4342) << 7) | (__byte_perm(sm.x, 0, 0x3322) & M);
-  o.z = (__byte_perm(ex.y, 0, 0x4140) << 7) | (__byte_perm(sm.y, 0, 0x1100) & M);
-  o.w = (__byte_perm(ex.y, 0, 0x4342) << 7) | (__byte_perm(sm.y, 0, 0x3322) & M);
+  // the fields are disjoint, so e * 128 + rest == e << 7 | rest
+  o.x = __byte_perm(ex.x, 0, 0x4140) * 128u + (__byte_perm(sm.x, 0, 0x1100) & M);
+  o.y = __byte_perm(ex.x, 0, 0x4342) * 128u + (__byte_perm(sm.x, 0, 0x3322) & M);
+  o.z = __byte_perm(ex.y, 0, 0x4140) * 128u + (__byte_perm(sm.y, 0, 0x1100) & M);
+  o.w = __byte_perm(ex.y, 0, 0x4342) * 128u + (__byte_perm(sm.y, 0, 0x3322) & M);
   return o;
 }
 
@@ -293,14 +301,16 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// Per-lane bit reader over one chunk: a 64-bit MSB-aligned buffer `acc`
-// holding `nb` valid bits, fed 32 bits at a time from the current 16-byte
-// block (big-endian words q0..q3, `qn` left). Blocks stream through a
-// per-lane shared-memory ring of kSlots 16-byte slots: kSlots - 1 copies are
-// always in flight, so a block is requested ~(kSlots - 1) * 16 bytes before
-// the lane reaches it.
+// Per-lane bit reader over one chunk: a 64-bit MSB-aligned buffer held as
+// two 32-bit halves (ah:al) with `nb` valid bits, fed 32 bits at a time
+// from the current 16-byte block (big-endian words q0..q3, `qn` left).
+// Every shift amount is known to be below 32 (consumption <= 16 bits per
+// lookup, refills while nb < 32), so each step is a single funnel shift.
+// Blocks stream through a per-lane shared-memory ring of kSlots 16-byte
+// slots: kSlots - 1 copies are always in flight, so a block is requested
+// ~(kSlots - 1) * 16 bytes before the lane reaches it.
 struct Reader {
-  uint64_t acc;
+  uint32_t ah, al;
   int nb;
   uint32_t q0, q1, q2, q3;
   int qn;
@@ -320,12 +330,21 @@ __device__ __forceinline__ void reader_next_block(Reader &r, unsigned char *ring
   r.slot = (r.slot + 1) & (kSlots - 1);
 }
 
+// nb < 32: append the next word below the valid bits
 __device__ __forceinline__ void reader_refill(Reader &r, unsigned char *ring, const uint4 *src, int64_t bmax,
                                               uint64_t pol) {
-  r.acc |= static_cast<uint64_t>(r.q0) << (32 - r.nb);
+  r.ah |= r.q0 >> r.nb;
+  r.al |= __funnelshift_r(0u, r.q0, static_cast<uint32_t>(r.nb));  // q0 << (32 - nb); 0 when nb == 0
   r.nb += 32;
   r.q0 = r.q1; r.q1 = r.q2; r.q2 = r.q3;
   if (--r.qn == 0) reader_next_block(r, ring, src, bmax, pol);
+}
+
+// drop `n` (< 32) consumed bits
+__device__ __forceinline__ void reader_consume(Reader &r, uint32_t n) {
+  r.ah = __funnelshift_l(r.al, r.ah, n);
+  r.al <<= n;
+  r.nb -= static_cast<int>(n);
 }
 
 __device__ __forceinline__ void reader_init(Reader &r, unsigned char *ring, const uint4 *src, int64_t bmax,
@@ -340,17 +359,35 @@ __device__ __forceinline__ void reader_init(Reader &r, unsigned char *ring, cons
   if (wofs & 2) { uint32_t t0 = r.q0, t1 = r.q1; r.q0 = r.q2; r.q1 = r.q3; r.q2 = t0; r.q3 = t1; }
   if (wofs & 1) { uint32_t t0 = r.q0; r.q0 = r.q1; r.q1 = r.q2; r.q2 = r.q3; r.q3 = t0; }
   r.qn = 4 - wofs;
-  r.acc = 0;
+  r.ah = 0;
+  r.al = 0;
   r.nb = 0;
   reader_refill(r, ring, src, bmax, pol);  // first word, then drop the bytes before the chunk start
-  const int skip = static_cast<int>(pos & 3) * 8;
-  r.acc <<= skip;
-  r.nb -= skip;
+  reader_consume(r, static_cast<uint32_t>(pos & 3) * 8);
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ Batch batch,
-                                                          int32_t *status) {
+// Append one table payload (up to four symbols, 8 * count in e.y bits
+// 8..15) to the lane's pending bytes olo:ohi and flush a full word to the
+// ring. Payload bytes beyond the count are zero, so a zero entry is a no-op.
+__device__ __forceinline__ void emit(uint2 e, uint32_t &olo, uint32_t &ohi, int &n8, int &k,
+                                     unsigned char *my_ring) {
+  olo |= e.x << n8;
+  ohi |= __funnelshift_l(e.x, 0u, static_cast<uint32_t>(n8));
+  n8 += static_cast<int>(e.y >> 8);
+  if (n8 >= 32) {
+    *reinterpret_cast<uint32_t *>(my_ring + (k & (kRing - 1))) = olo;
+    olo = ohi;
+    ohi = 0;
+    n8 -= 32;
+    k += 4;
+  }
+}
+
+// CSC != 0 specialises the kernel for one chunk size (the reference's
+// default, 1024), making the merge's address offsets compile-time constants.
+template <int MODE, int CSC>
+__global__ void __launch_bounds__(kThreads, AIB_MIN_BLOCKS) decode_kernel(const __grid_constant__ Batch batch,
+                                                                          int32_t *status) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ uint64_t bar;
 
@@ -394,7 +431,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   unsigned char *ring_base = smem + kFastBytes + warp * kRingWarpBytes;
   unsigned char *my_ring = ring_base + lane * kRow;
   unsigned char *my_stream = smem + kFastBytes + kWarps * kRingWarpBytes + warp * kStreamWarpBytes + lane * kSlotRow;
-  const int64_t cs = J.chunk_size;
+  const int64_t cs = CSC ? static_cast<int64_t>(CSC) : static_cast<int64_t>(J.chunk_size);
   const int max_bits = J.max_bits;
   const uint4 *src = reinterpret_cast<const uint4 *>(J.packed);
   const int64_t bmax = J.packed_cap / 16 - 1;
@@ -420,7 +457,7 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     const int need = active ? static_cast<int>(min(cs, J.e1 - c * cs)) : 0;
 
     Reader rd;
-    rd.acc = 0; rd.nb = 0; rd.q0 = rd.q1 = rd.q2 = rd.q3 = 0; rd.qn = 4; rd.bi = 0;
+    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.q0 = rd.q1 = rd.q2 = rd.q3 = 0; rd.qn = 4; rd.bi = 0;
     rd.slot = 0;
     if (active) {
       int64_t pos = static_cast<int64_t>(J.offs[c - J.chunk_base]) - J.offset_base;
@@ -451,34 +488,43 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         if (ph + kPhase < max_need) prefetch_l2(J.sm + grp_out + static_cast<int64_t>(lane) * cs + ph + kPhase);
       }
       const int target = min(ph + kPhase, need);
-      while (k + (n8 >> 3) < target) {
-        if (rd.nb < 32) reader_refill(rd, my_stream, src, bmax, pol_keep);
+#if AIB_AHEAD
+      // Lanes that reach this phase's target keep decoding into the ring's
+      // slack (up to `cap`, never into the region still to be merged), so a
+      // warp waits on its slowest lane once per chunk rather than per phase.
+      const int cap = min(ph + kRing - 12, need);
+      while (__any_sync(0xffffffffu, k + (n8 >> 3) < target)) {
+        if (k + (n8 >> 3) < cap) {
+#else
+      {
+        while (k + (n8 >> 3) < target) {
+#endif
+          if (rd.nb < 32) reader_refill(rd, my_stream, src, bmax, pol_keep);
+          // Two first-level lookups. A window whose first code is longer
+          // than the table (entry 0, a no-op) is resolved below by the
+          // reference LUT, outside the common path.
+          uint32_t ymin = 0xFFFFFFFFu;
 #pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          uint2 e = s_fast[static_cast<uint32_t>(rd.acc >> (64 - kFastBits))];
-          if (e.y == 0u) {
-            // code longer than the first level: the reference LUT lookup
-            const uint32_t w = (static_cast<uint32_t>(rd.acc >> 48)) >> (16 - max_bits);
-            const uint32_t s = static_cast<uint32_t>(__ldg(J.sym_lut + w)) & 0xFFu;
-            const uint32_t l = static_cast<uint32_t>(static_cast<int>(__ldg(J.len_lut + w))) & 31u;
-            e = make_uint2(s, l | (8u << 8));
+          for (int u = 0; u < 2; ++u) {
+            const uint2 e = s_fast[rd.ah >> (32 - kFastBits)];
+            ymin = min(ymin, e.y);
+            reader_consume(rd, e.y & 31u);
+            emit(e, olo, ohi, n8, k, my_ring);
           }
-          const uint32_t used = e.y & 31u;
-          rd.acc <<= used;
-          rd.nb -= static_cast<int>(used);
-          olo |= e.x << n8;
-          ohi |= __funnelshift_l(e.x, 0u, static_cast<uint32_t>(n8));
-          n8 += static_cast<int>(e.y >> 8);
-          if (n8 >= 32) {
-            *reinterpret_cast<uint32_t *>(my_ring + (k & (kRing - 1))) = olo;
-            olo = ohi;
-            ohi = 0;
-            n8 -= 32;
-            k += 4;
+          if (__any_sync(__activemask(), ymin == 0u)) {
+            if (ymin == 0u) {
+              // >= 20 valid bits remain here: the window needs max_bits <= 16
+              const uint32_t w = (rd.ah >> 16) >> (16 - max_bits);
+              const uint32_t sy = static_cast<uint32_t>(__ldg(J.sym_lut + w)) & 0xFFu;
+              const uint32_t l = static_cast<uint32_t>(static_cast<int>(__ldg(J.len_lut + w))) & 31u;
+              reader_consume(rd, l);
+              emit(make_uint2(sy, 8u << 8), olo, ohi, n8, k, my_ring);
+            }
           }
         }
       }
-      if (k < target)  // end of this lane's range: flush the partial word
+      // end of this lane's range: flush the partial word (idempotent)
+      if (k < need && k + (n8 >> 3) >= need)
         *reinterpret_cast<uint32_t *>(my_ring + (k & (kRing - 1))) = olo;
       __syncwarp();
 
@@ -583,13 +629,21 @@ struct DeviceInfo {
 static DeviceInfo g_dev[64];
 static std::mutex g_dev_mu;
 
+template <int MODE, int CSC>
+static int setup_one(DeviceInfo &di) {
+  AIB_CUDA(cudaFuncSetAttribute(decode_kernel<MODE, CSC>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
+  int occ = 0;
+  AIB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<MODE, CSC>, kThreads, kSmemBytes));
+  di.occ[MODE] = di.occ[MODE] ? std::min(di.occ[MODE], std::max(1, occ)) : std::max(1, occ);
+  return AIB_OK;
+}
+
 template <int MODE>
 static int setup_kernel(int dev, DeviceInfo &di) {
-  AIB_CUDA(cudaFuncSetAttribute(decode_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
-  int occ = 0;
-  AIB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, decode_kernel<MODE>, kThreads, kSmemBytes));
-  di.occ[MODE] = std::max(1, occ);
-  return AIB_OK;
+  (void)dev;
+  int rc = setup_one<MODE, 0>(di);
+  if (rc == AIB_OK) rc = setup_one<MODE, kDefaultChunk>(di);
+  return rc;
 }
 
 static int device_info(DeviceInfo **out) {
@@ -729,7 +783,12 @@ static int launch(const aib_stream_desc *descs, int count, int32_t *status, void
     j.ctas = static_cast<int32_t>(share);
     cta += j.ctas;
   }
-  decode_kernel<MODE><<<cta, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(batch, status);
+  bool all_default = true;
+  for (int i = 0; i < n; ++i) all_default = all_default && batch.job[i].chunk_size == kDefaultChunk;
+  if (all_default)
+    decode_kernel<MODE, kDefaultChunk><<<cta, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(batch, status);
+  else
+    decode_kernel<MODE, 0><<<cta, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(batch, status);
   AIB_CUDA(cudaGetLastError());
   return AIB_OK;
 }
