@@ -31,6 +31,7 @@ import pathlib
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import numpy as np
@@ -85,11 +86,10 @@ class Clocks:
     def __init__(self, index: int):
         self.index = index
         self.proc = None
-        self.path = ROOT / "gpurun_out" / f".clocks_{os.getpid()}.csv"
+        self.path = pathlib.Path(tempfile.gettempdir()) / f"aib_clocks_{os.getpid()}.csv"
 
     def __enter__(self):
         try:
-            self.path.parent.mkdir(exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
                                           "-i", str(self.index), "-lms", "200"], stdout=self.fh,
@@ -231,7 +231,7 @@ def run_reference(args, world, rank):
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=2000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--workload", default="qwen3-14b-layer", choices=sorted(WORKLOADS))

@@ -1,9 +1,10 @@
 """Generates the golden fixtures in this directory by running the REFERENCE
 implementation (Afterimage 0.3.0's own encoder and decoders).
 
-Run in a container where the reference tree is available:
+Run where a checkout of the reference is available:
 
-    AFTERIMAGE_REF=/path/to/afterimage-checkout python tests/golden/make_golden.py
+    python tests/golden/make_golden.py /path/to/afterimage-checkout
+    (or set AFTERIMAGE_REF to that path)
 
 It imports the reference read-only (no bytecode written, numba cache
 redirected to a temp dir) and writes:
@@ -37,7 +38,10 @@ os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
 os.environ.setdefault("NUMBA_CACHE_DIR", tempfile.mkdtemp(prefix="numba_golden_"))
 sys.dont_write_bytecode = True
 
-REF = pathlib.Path(os.environ.get("AFTERIMAGE_REF", "/root/reference"))
+_ref_arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("AFTERIMAGE_REF")
+if not _ref_arg:
+    raise SystemExit("usage: make_golden.py <path to an Afterimage checkout> (or set AFTERIMAGE_REF)")
+REF = pathlib.Path(_ref_arg)
 sys.path.insert(0, str(REF))
 
 import numpy as np  # noqa: E402
