@@ -1,0 +1,84 @@
+"""Offline compression and store checks that need no GPU: the store layout
+follows the reference's per-tensor rules (streaming_engine.py:158-253,
+:362-427), every compressed tensor round-trips through the oracle, and the
+engine refuses bad stores before touching a device."""
+import json
+import shutil
+
+import numpy as np
+import pytest
+import torch
+
+from test_streaming_engine_gpu import _store, _tiny
+from oracle import oracle as O
+from afterimage_b200.runtime.binstore import BinaryWeightReader
+from afterimage_b200.runtime.huffman_chunked import ChunkedEncoded
+
+
+@pytest.fixture(scope="module")
+def untied_store(tmp_path_factory):
+    tmp = tmp_path_factory.mktemp("store")
+    cfg, model = _tiny(tie=False, seed=1)
+    snap, store, manifest = _store(tmp, cfg, model, "u")
+    return cfg, model, snap, store, manifest
+
+
+def test_store_layout_matches_reference_rules(untied_store):
+    cfg, model, snap, store, m = untied_store
+    assert m["schema_version"] == 2 and m["tied"] is False
+    t = m["tensors"]
+    assert t["model.embed_tokens.weight"]["row_gather"] is True
+    assert t["model.embed_tokens.weight"]["hidden_size"] == cfg.hidden_size
+    assert t["model.layers.0.mlp.gate_proj.weight"]["compressed"] is True
+    assert t["model.layers.0.self_attn.k_proj.weight"]["compressed"] is False  # 160x320 <= 65536
+    assert t["model.layers.0.input_layernorm.weight"]["dtype"] == "torch.bfloat16"
+    assert set(t["model.layers.0.mlp.gate_proj.weight"]["blobs"]) == {
+        "sign_mantissa", "packed", "chunk_offsets", "chunk_nbytes", "sym_lut", "len_lut"}
+    assert m["total_orig_bytes"] == sum(v["orig_bytes"] for v in t.values())
+
+
+def test_every_stored_tensor_round_trips_through_the_oracle(untied_store):
+    cfg, model, snap, store, m = untied_store
+    sd = model.state_dict()
+    with BinaryWeightReader(store / "weights.bin") as r:
+        for key, meta in m["tensors"].items():
+            blobs = {n: r.read(ref, verify=True) for n, ref in meta["blobs"].items()}
+            want = sd[key].view(torch.int16).reshape(-1).numpy()
+            if meta.get("compressed"):
+                n = meta["n_symbols"]
+                enc = ChunkedEncoded(packed=blobs["packed"], chunk_offsets=blobs["chunk_offsets"],
+                                     chunk_nbytes=blobs["chunk_nbytes"], sym_lut=blobs["sym_lut"],
+                                     len_lut=blobs["len_lut"], max_bits=meta["max_bits"],
+                                     chunk_size=meta["chunk_size"], n_symbols=n, shape=(n,))
+                got = O.decompress(enc, blobs["sign_mantissa"]).view(np.int16)
+            elif meta.get("row_gather"):
+                got = blobs["raw"].reshape(-1)
+            else:
+                got = torch.from_numpy(blobs["raw"]).to(torch.bfloat16).view(torch.int16).reshape(-1).numpy()
+            assert np.array_equal(got, want), key
+
+
+def test_engine_rejects_bad_schema_and_truncated_store_before_any_device_use(untied_store, tmp_path):
+    from afterimage_b200.runtime.streaming_engine import StreamingLosslessModel
+    cfg, model, snap, store, _ = untied_store
+    bad = tmp_path / "bad"
+    shutil.copytree(store, bad)
+    m = json.loads((bad / "manifest.json").read_text())
+    m["schema_version"] = 1
+    (bad / "manifest.json").write_text(json.dumps(m))
+    with pytest.raises(RuntimeError, match="schema_version"):
+        StreamingLosslessModel(str(snap), bad)
+    m["schema_version"] = 2
+    (bad / "manifest.json").write_text(json.dumps(m))
+    with open(bad / "weights.bin", "r+b") as f:
+        f.truncate(100)
+    with pytest.raises(RuntimeError, match="truncated"):
+        StreamingLosslessModel(str(snap), bad)
+
+
+def test_engine_config_validation():
+    from afterimage_b200.runtime.streaming_engine import EngineConfig
+    for bad in (dict(chunk_size=0), dict(max_bits=17), dict(io_prefetch_depth=-1),
+                dict(ram_tier_format="x"), dict(vram_tier_format="y"), dict(ram_budget_gb=1.0)):
+        with pytest.raises(ValueError):
+            EngineConfig(**bad)

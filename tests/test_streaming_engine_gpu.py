@@ -1,0 +1,149 @@
+"""End-to-end engine tests on tiny random Qwen3/Llama checkpoints (no
+network): the streaming engine's logits and greedy tokens must equal a plain
+in-memory transformers forward on the same weights, bit for bit, across
+tiers, prefetch depths, tied/untied heads, KV cache and draft speculation
+(the reference's tests/test_streaming_engine_gpu.py, restated)."""
+import pytest
+import torch
+from safetensors.torch import save_file
+
+pytestmark = pytest.mark.gpu
+
+
+def _tiny(tie=False, seed=0, arch="qwen3", layers=3, vocab=1536):
+    from transformers import AutoModelForCausalLM, LlamaConfig, Qwen3Config
+    torch.manual_seed(seed)
+    common = dict(vocab_size=vocab, hidden_size=320, intermediate_size=896, num_hidden_layers=layers,
+                  num_attention_heads=4, num_key_value_heads=2, head_dim=80, max_position_embeddings=128,
+                  tie_word_embeddings=tie)
+    cfg = Qwen3Config(**common) if arch == "qwen3" else LlamaConfig(**common)
+    model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16)
+    with torch.no_grad():  # N(0, 0.02)-like weights with real exponent spread
+        for p in model.parameters():
+            if p.dim() == 2:
+                p.normal_(0, 0.02)
+    return cfg, model.eval()
+
+
+def _store(tmp_path, cfg, model, tag, **kw):
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, compress_model_to_disk
+    snap = tmp_path / ("snap_" + tag)
+    snap.mkdir()
+    sd = {k: v.contiguous() for k, v in model.state_dict().items()}
+    if cfg.tie_word_embeddings:
+        sd.pop("lm_head.weight", None)
+    save_file(sd, str(snap / "model.safetensors"))
+    cfg.save_pretrained(snap)
+    store = tmp_path / ("store_" + tag)
+    m = compress_model_to_disk(str(snap), store, config=EngineConfig(chunk_size=256, **kw))
+    return snap, store, m
+
+
+def _engine(snap, store, **kw):
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, StreamingLosslessModel
+    return StreamingLosslessModel(str(snap), store, device="cuda", config=EngineConfig(**kw))
+
+
+@pytest.fixture(scope="module")
+def untied(tmp_path_factory):
+    tmp = tmp_path_factory.mktemp("untied")
+    cfg, model = _tiny(tie=False, seed=1)
+    snap, store, manifest = _store(tmp, cfg, model, "u")
+    return cfg, model.to("cuda"), snap, store, manifest
+
+
+@pytest.mark.parametrize("depth", [0, 1, 2])
+def test_logits_bit_exact_vs_plain_forward(untied, depth):
+    cfg, model, snap, store, _ = untied
+    ids = torch.randint(0, cfg.vocab_size, (1, 7), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits
+    with _engine(snap, store, io_prefetch_depth=depth) as eng:
+        got = eng.forward_logits(ids)
+        got2 = eng.forward_logits(ids)
+        assert eng.stats.decode_launches > 0
+    assert torch.equal(got, ref) and torch.equal(got2, ref)
+
+
+@pytest.mark.parametrize("tiers", [
+    dict(vram=0.3, ram=0.0), dict(vram=0.3, ram=0.3), dict(vram=0.3, ram=0.3, ram_tier_format="compressed"),
+    dict(vram=0.6, vram_tier_format="compressed"), dict(vram=2.0),
+])
+def test_tiered_residency_is_bit_exact(untied, tiers):
+    """Budgets are set as a fraction of the model's bytes above the
+    planner's fixed headroom, so the cases mix VRAM, RAM and disk tiers."""
+    from afterimage_b200.runtime.vram_planner import DEFAULT_ACTIVATION_SLACK_BYTES, decode_scratch_bytes
+    cfg, model, snap, store, manifest = untied
+    t = {k: v for k, v in manifest["tensors"].items() if not v.get("row_gather")}
+    total = sum(v["orig_bytes"] for v in t.values())
+    slice_elems = 1 << 16
+    head = max(v["orig_bytes"] for v in t.values()) + decode_scratch_bytes(slice_elems) + DEFAULT_ACTIVATION_SLACK_BYTES
+    kw = dict(tiers)
+    kw["vram_budget_gb"] = (head + kw.pop("vram") * total) / 1e9
+    if "ram" in kw:
+        kw["ram_budget_gb"] = kw.pop("ram") * total / 1e9
+    ids = torch.randint(0, cfg.vocab_size, (1, 5), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits
+    with _engine(snap, store, decode_slice_elems=slice_elems, **kw) as eng:
+        got = eng.forward_logits(ids)
+        got2 = eng.forward_logits(ids)
+        kinds = sorted(set(eng._tier.values()))
+    assert torch.equal(got, ref) and torch.equal(got2, ref), kinds
+    if tiers.get("vram", 0) < 1:
+        assert "disk" in kinds or "ram" in kinds, kinds
+
+
+def test_greedy_matches_reference_argmax_loop_and_kv_cache(untied):
+    cfg, model, snap, store, _ = untied
+    ids = torch.randint(0, cfg.vocab_size, (1, 6), device="cuda")
+    seq = ids
+    with torch.no_grad():
+        for _ in range(5):
+            nxt = model(input_ids=seq).logits[:, -1, :].argmax(-1, keepdim=True)
+            seq = torch.cat([seq, nxt], 1)
+    seen = []
+    with _engine(snap, store) as eng:
+        cached = eng.generate_greedy(ids, 5, use_cache=True, on_token=seen.append)
+        full = eng.generate_greedy(ids, 5, use_cache=False)
+        stop = int(seq[0, 7])
+        stopped = eng.generate_greedy(ids, 5, stop_token_ids=(stop,))
+    assert torch.equal(cached, seq) and torch.equal(full, seq)
+    assert seen == seq[0, 6:].tolist()
+    first = 6 + seq[0, 6:].tolist().index(stop)  # generation stops at the first occurrence
+    assert torch.equal(stopped, seq[:, :first + 1])
+
+
+def test_tied_model_uses_compressed_embedding_as_head(tmp_path):
+    cfg, model = _tiny(tie=True, seed=2)
+    snap, store, m = _store(tmp_path, cfg, model, "t")
+    assert "lm_head.weight" not in m["tensors"] and m["tensors"]["model.embed_tokens.weight"]["compressed"]
+    model = model.to("cuda")
+    ids = torch.randint(0, cfg.vocab_size, (1, 9), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits
+    with _engine(snap, store, io_prefetch_depth=1) as eng:
+        assert torch.equal(eng.forward_logits(ids), ref)
+
+
+def test_llama_layout_streams_bit_exact(tmp_path):
+    cfg, model = _tiny(seed=3, arch="llama")
+    snap, store, _ = _store(tmp_path, cfg, model, "l")
+    model = model.to("cuda")
+    ids = torch.randint(0, cfg.vocab_size, (1, 4), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits
+    with _engine(snap, store, io_prefetch_depth=2) as eng:
+        assert torch.equal(eng.forward_logits(ids), ref)
+
+
+def test_draft_speculation_at_temperature_zero_equals_greedy(untied, tmp_path):
+    cfg, model, snap, store, _ = untied
+    _, draft = _tiny(tie=True, seed=9, layers=1)
+    draft = draft.to("cuda")
+    ids = torch.randint(0, cfg.vocab_size, (1, 5), device="cuda")
+    with _engine(snap, store) as eng:
+        greedy = eng.generate_greedy(ids, 7)
+        spec = eng.generate_speculative(ids, 7, draft, k=3, temperature=0.0)
+        assert eng.stats.spec_sweeps >= 1
+    assert torch.equal(spec, greedy)
