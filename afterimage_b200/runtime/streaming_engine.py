@@ -21,9 +21,9 @@ What the B200 build does differently on the per-layer path:
   * decode tables are built once per tensor and stay on the device;
   * nothing synchronises the device per layer: buffers are returned to the
     caching allocator in stream order.
-Extra tier: `vram_tier_format="compressed"` keeps VRAM-tier tensors in
-their compressed form in HBM and decodes them per layer -- ~1.5x more model
-per GB of HBM at the cost of one decode per use.
+Extra tier: `vram_tier_format="compressed"` keeps VRAM-tier decoder-layer
+tensors in their compressed form in HBM and decodes them per layer -- ~1.5x
+more model per GB of HBM at the cost of one decode per use.
 """
 from __future__ import annotations
 
@@ -170,43 +170,22 @@ def compress_one_tensor(key: str, W: torch.Tensor, cfg: EngineConfig, row_gather
             "comp_bytes": orig, "arrays": {"raw": W.to(torch.float32).numpy()}}
 
 
-def compress_model_to_disk(model_id: str, out_dir, config: EngineConfig | None = None, progress_every: int = 50,
-                           source_dir=None, revision: str | None = None, hf_config=None) -> dict:
-    """safetensors -> one `weights.bin` + `manifest.json` (schema v2),
-    readable by the reference engine and by this one (reference
-    streaming_engine.py:256-428). The encoder is multi-threaded C++, so
-    tensors are compressed in-process in checkpoint order (embedding and
-    head first, as the reference writes them)."""
-    from safetensors import safe_open
-
+def write_store(items, out_dir, config: EngineConfig | None = None, *, tied: bool, model_id: str = "",
+                revision: str | None = None, progress_every: int = 50, total: int | None = None) -> dict:
+    """Writes a compressed store from an iterable of (key, tensor) pairs:
+    `weights.bin` + schema-v2 `manifest.json` (reference
+    streaming_engine.py:345-427). The untied embedding is stored raw and
+    row-addressable; each tensor is released after it is written."""
     cfg = config or EngineConfig()
     out_dir = pathlib.Path(out_dir)
     out_dir.mkdir(parents=True, exist_ok=True)
-    snap = _resolve_snapshot(model_id, source_dir, revision)
-    shards = _weight_shards(snap)
-    if not shards:
-        raise FileNotFoundError("no .safetensors in " + str(snap))
-    if hf_config is None:
-        from transformers import AutoConfig
-        hf_config = AutoConfig.from_pretrained(snap, trust_remote_code=False)
-    tied = bool(getattr(hf_config, "tie_word_embeddings", False))
     row_gather_key = None if tied else "model.embed_tokens.weight"
-
-    tasks = []
-    for shard in shards:
-        with safe_open(str(shard), framework="pt", device="cpu") as f:
-            tasks.extend((str(shard), key) for key in f.keys())
-    tasks = ([t for t in tasks if t[1].endswith(_BIG_TENSOR_SUFFIXES)]
-             + [t for t in tasks if not t[1].endswith(_BIG_TENSOR_SUFFIXES)])
-
     manifest = {"schema_version": CURRENT_SCHEMA_VERSION, "model_id": model_id, "revision": revision,
                 "quantize": None, "chunk_size": cfg.chunk_size, "force_raw_storage": cfg.force_raw_storage,
                 "tied": tied, "tensors": {}, "expert_slices": {}}
     total_orig = total_comp = 0
     with BinaryWeightWriter(out_dir / "weights.bin") as writer:
-        for n, (shard, key) in enumerate(tasks, 1):
-            with safe_open(shard, framework="pt", device="cpu") as f:
-                W = f.get_tensor(key)
+        for n, (key, W) in enumerate(items, 1):
             res = compress_one_tensor(key, W, cfg, row_gather=(key == row_gather_key))
             del W
             entry = {"orig_bytes": res["orig_bytes"], "comp_bytes": res["comp_bytes"], "shape": res["shape"],
@@ -221,14 +200,47 @@ def compress_model_to_disk(model_id: str, out_dir, config: EngineConfig | None =
             manifest["tensors"][key] = entry
             total_orig += res["orig_bytes"]
             total_comp += res["comp_bytes"]
+            del res
             if progress_every and n % progress_every == 0:
-                print("  [%d/%d] %.2f GB -> %.2f GB" % (n, len(tasks), total_orig / 1e9, total_comp / 1e9),
+                print("  [%d/%s] %.2f GB -> %.2f GB" % (n, total or "?", total_orig / 1e9, total_comp / 1e9),
                       flush=True)
     manifest["total_orig_bytes"] = total_orig
     manifest["total_comp_bytes"] = total_comp
     manifest["ratio"] = total_orig / max(total_comp, 1)
     (out_dir / "manifest.json").write_text(json.dumps(manifest, indent=2), encoding="utf-8", newline="\n")
     return manifest
+
+
+def compress_model_to_disk(model_id: str, out_dir, config: EngineConfig | None = None, progress_every: int = 50,
+                           source_dir=None, revision: str | None = None, hf_config=None) -> dict:
+    """safetensors -> one `weights.bin` + `manifest.json` (schema v2),
+    readable by the reference engine and by this one (reference
+    streaming_engine.py:256-428). The encoder is multi-threaded C++, so
+    tensors are compressed in-process in checkpoint order (embedding and
+    head first, as the reference writes them)."""
+    from safetensors import safe_open
+
+    snap = _resolve_snapshot(model_id, source_dir, revision)
+    shards = _weight_shards(snap)
+    if not shards:
+        raise FileNotFoundError("no .safetensors in " + str(snap))
+    if hf_config is None:
+        from transformers import AutoConfig
+        hf_config = AutoConfig.from_pretrained(snap, trust_remote_code=False)
+    tasks = []
+    for shard in shards:
+        with safe_open(str(shard), framework="pt", device="cpu") as f:
+            tasks.extend((str(shard), key) for key in f.keys())
+    tasks = ([t for t in tasks if t[1].endswith(_BIG_TENSOR_SUFFIXES)]
+             + [t for t in tasks if not t[1].endswith(_BIG_TENSOR_SUFFIXES)])
+
+    def items():
+        for shard, key in tasks:
+            with safe_open(shard, framework="pt", device="cpu") as f:
+                yield key, f.get_tensor(key)
+
+    return write_store(items(), out_dir, config, tied=bool(getattr(hf_config, "tie_word_embeddings", False)),
+                       model_id=model_id, revision=revision, progress_every=progress_every, total=len(tasks))
 
 
 # ---------------------------------------------------------------------------
@@ -472,7 +484,8 @@ class StreamingLosslessModel:
                     continue
                 arrays = self._read_arrays([key], self._reader, pinned=False)[key]
                 if tier == "vram":
-                    if self.config.vram_tier_format == "compressed" and meta["compressed"]:
+                    if (self.config.vram_tier_format == "compressed" and meta["compressed"]
+                            and key.startswith("model.layers.")):
                         self._vram_compressed[key] = upload_layer(_encoded_from_arrays(meta, arrays), self.device)
                     else:
                         _set_param(self.model, key, self._decode_whole(key, arrays))
