@@ -171,11 +171,17 @@ def compress_one_tensor(key: str, W: torch.Tensor, cfg: EngineConfig, row_gather
 
 
 def write_store(items, out_dir, config: EngineConfig | None = None, *, tied: bool, model_id: str = "",
-                revision: str | None = None, progress_every: int = 50, total: int | None = None) -> dict:
+                revision: str | None = None, progress_every: int = 50, total: int | None = None,
+                tp_row_chunks: int | None = None) -> dict:
     """Writes a compressed store from an iterable of (key, tensor) pairs:
     `weights.bin` + schema-v2 `manifest.json` (reference
     streaming_engine.py:345-427). The untied embedding is stored raw and
-    row-addressable; each tensor is released after it is written."""
+    row-addressable; each tensor is released after it is written.
+
+    tp_row_chunks=P makes the store tensor-parallel ready: the row-parallel
+    projections (o_proj, down_proj) use chunk_size = in_features / P, so
+    each of P (or any divisor of P) ranks owns whole chunks of every row.
+    The format is unchanged (chunk_size is per tensor)."""
     cfg = config or EngineConfig()
     out_dir = pathlib.Path(out_dir)
     out_dir.mkdir(parents=True, exist_ok=True)
@@ -186,7 +192,11 @@ def write_store(items, out_dir, config: EngineConfig | None = None, *, tied: boo
     total_orig = total_comp = 0
     with BinaryWeightWriter(out_dir / "weights.bin") as writer:
         for n, (key, W) in enumerate(items, 1):
-            res = compress_one_tensor(key, W, cfg, row_gather=(key == row_gather_key))
+            tcfg = cfg
+            if (tp_row_chunks and W.dim() == 2 and key.endswith(("o_proj.weight", "down_proj.weight"))
+                    and W.shape[1] % tp_row_chunks == 0):
+                tcfg = dataclasses.replace(cfg, chunk_size=W.shape[1] // tp_row_chunks)
+            res = compress_one_tensor(key, W, tcfg, row_gather=(key == row_gather_key))
             del W
             entry = {"orig_bytes": res["orig_bytes"], "comp_bytes": res["comp_bytes"], "shape": res["shape"],
                      "blobs": {name: blobref_to_dict(writer.write(arr)) for name, arr in res["arrays"].items()}}

@@ -1,0 +1,385 @@
+"""Tensor-parallel decoder over compressed weights (Qwen3 / Llama layouts).
+
+Sharding (one process per GPU, torch.distributed / NCCL):
+  * column-parallel: q_proj, k_proj, v_proj, gate_proj, up_proj and the
+    vocab rows of lm_head -- rank r owns output rows [r*out/P, (r+1)*out/P),
+    i.e. a contiguous run of whole chunks when the row length is a multiple
+    of chunk_size, decoded with the element-range decode;
+  * row-parallel: o_proj, down_proj -- rank r owns input columns
+    [r*in/P, (r+1)*in/P) of every row. A TP-ready store compresses these
+    tensors with chunk_size = in/P_max (write_store(tp_row_chunks=...)) so a
+    rank's columns are whole chunks, gathered into a flat stream; for other
+    chunk sizes the rank decodes the covering chunks of each row and slices;
+  * one all-reduce (sum) after o_proj and one after down_proj per layer,
+    an all-gather of the vocab shards for logits.
+Heads divide across ranks (num_attention_heads and num_key_value_heads must
+be multiples of P). The math mirrors transformers' Qwen3/Llama modules:
+float32 RMSNorm, rotate-half RoPE with float32 cos/sin, SDPA attention.
+
+Weights live on each rank either decoded (BF16 shards) or compressed
+(`resident="compressed"`: the shard's compressed stream in HBM, decoded per
+layer per forward by one batched launch).
+"""
+from __future__ import annotations
+
+import dataclasses
+import json
+import math
+import pathlib
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import _device
+from .binstore import BinaryWeightReader
+from .compressed_store import CompressedLayer
+from .huffman_chunked import ChunkedEncoded
+from .layer_decode import LayerDecoder, upload_layer
+
+COL_PARALLEL = ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj")
+ROW_PARALLEL = ("o_proj", "down_proj")
+
+
+def shard_kind(key: str) -> str:
+    name = key.rsplit(".", 2)[-2] if key.count(".") >= 2 else key
+    if key == "lm_head.weight":
+        return "col"
+    if name in COL_PARALLEL:
+        return "col"
+    if name in ROW_PARALLEL:
+        return "row"
+    return "rep"
+
+
+def _split(n: int, world: int, rank: int) -> tuple[int, int]:
+    if n % world:
+        raise ValueError(f"dimension {n} does not divide across {world} ranks")
+    s = n // world
+    return rank * s, (rank + 1) * s
+
+
+@dataclasses.dataclass
+class ShardStream:
+    """A rank's shard as a flat compressed stream plus how to finish it:
+    decode `layer` (flat), take `rows * cols_decoded` elements from
+    `elem_lo`, view them as [rows, cols_decoded] and keep columns
+    [col_lo, col_lo + cols). Shards made of whole chunks need no slicing
+    (elem_lo = col_lo = 0, cols = cols_decoded)."""
+    layer: CompressedLayer
+    rows: int
+    cols_decoded: int
+    col_lo: int
+    cols: int
+    elem_lo: int = 0
+
+    @property
+    def exact(self) -> bool:
+        return self.elem_lo == 0 and self.col_lo == 0 and self.cols == self.cols_decoded and \
+            int(self.layer.encoded.n_symbols) == self.rows * self.cols_decoded
+
+    def finish(self, flat: torch.Tensor) -> torch.Tensor:
+        v = flat.reshape(-1)[self.elem_lo:self.elem_lo + self.rows * self.cols_decoded]
+        v = v.view(self.rows, self.cols_decoded)
+        if self.col_lo or self.cols != self.cols_decoded:
+            v = v[:, self.col_lo:self.col_lo + self.cols]
+        return v.contiguous()
+
+
+def _gather_chunks(enc, chunk_ids: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Packed bytes of the given chunks back to back, with rebased offsets."""
+    offs = np.asarray(enc.chunk_offsets, dtype=np.int64)[chunk_ids]
+    nbs = np.asarray(enc.chunk_nbytes, dtype=np.int64)[chunk_ids]
+    packed = np.asarray(enc.packed)
+    if len(chunk_ids) and np.all(np.diff(chunk_ids) == 1):
+        body = packed[offs[0]:offs[-1] + nbs[-1]]
+    else:
+        body = np.concatenate([packed[o:o + n] for o, n in zip(offs.tolist(), nbs.tolist())]) \
+            if len(chunk_ids) else np.zeros(0, np.uint8)
+    new_offs = np.zeros(len(chunk_ids), dtype=np.int32)
+    if len(chunk_ids) > 1:
+        new_offs[1:] = np.cumsum(nbs[:-1])
+    return np.concatenate([body, np.zeros(8, np.uint8)]), new_offs, nbs.astype(np.int32)
+
+
+def shard_stream(layer: CompressedLayer, kind: str, world: int, rank: int) -> ShardStream:
+    """The rank's shard of a 2-D compressed tensor as a flat stream
+    (host-side gather; nothing is decoded here)."""
+    enc = layer.encoded
+    rows, cols = layer.shape
+    cs = int(enc.chunk_size)
+    sm = layer.sign_mantissa.reshape(-1)
+    sm = sm.numpy() if isinstance(sm, torch.Tensor) else np.asarray(sm)
+    n = int(enc.n_symbols)
+    n_chunks = int(enc.n_chunks)
+    if kind == "col":
+        # output rows [r0, r1): a contiguous element range -> the chunks covering it
+        r0, r1 = _split(rows, world, rank)
+        e0, e1 = r0 * cols, r1 * cols
+        c_lo, c_hi = e0 // cs, min(n_chunks, -(-e1 // cs))
+        ids = np.arange(c_lo, c_hi, dtype=np.int64)
+        sm_s = sm[c_lo * cs:min(c_hi * cs, n)]
+        out_rows, dec_cols, lo, keep, elem_lo = r1 - r0, cols, 0, cols, e0 - c_lo * cs
+    elif kind == "row":
+        c0, c1 = _split(cols, world, rank)
+        if cols % cs == 0:
+            # each row's covering chunks (whole chunks when in/P is a multiple of chunk_size)
+            cpr = cols // cs
+            j0, j1 = c0 // cs, -(-c1 // cs)
+            ids = (np.arange(rows, dtype=np.int64)[:, None] * cpr + np.arange(j0, j1)[None, :]).reshape(-1)
+            sm_s = sm.reshape(rows, cols)[:, j0 * cs:j1 * cs].reshape(-1)
+            out_rows, dec_cols, lo, keep, elem_lo = rows, (j1 - j0) * cs, c0 - j0 * cs, c1 - c0, 0
+        else:
+            # chunks straddle rows: decode the whole tensor, keep the columns
+            ids = np.arange(n_chunks, dtype=np.int64)
+            sm_s = sm
+            out_rows, dec_cols, lo, keep, elem_lo = rows, cols, c0, c1 - c0, 0
+    else:
+        raise ValueError("unknown shard kind %r" % kind)
+    packed, offs, nbs = _gather_chunks(enc, ids)
+    n_dec = int(sm_s.shape[0])
+    enc_s = ChunkedEncoded(packed=packed, chunk_offsets=offs, chunk_nbytes=nbs, sym_lut=enc.sym_lut,
+                           len_lut=enc.len_lut, max_bits=enc.max_bits, chunk_size=cs, n_symbols=n_dec,
+                           shape=(n_dec,))
+    return ShardStream(CompressedLayer(sign_mantissa=torch.from_numpy(np.ascontiguousarray(sm_s)), encoded=enc_s,
+                                       shape=(n_dec,)), out_rows, dec_cols, lo, keep, elem_lo)
+
+
+def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    dt = x.dtype
+    h = x.to(torch.float32)
+    h = h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + eps)
+    return w * h.to(dt)
+
+
+def _rotate_half(x: torch.Tensor) -> torch.Tensor:
+    half = x.shape[-1] // 2
+    return torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+
+
+class KVCache:
+    """Static per-rank cache: [layers][2] tensors of [1, kv_heads_local, max_len, head_dim]."""
+
+    def __init__(self, n_layers, kv_heads, head_dim, max_len, device, dtype=torch.bfloat16):
+        self.k = [torch.zeros(1, kv_heads, max_len, head_dim, device=device, dtype=dtype) for _ in range(n_layers)]
+        self.v = [torch.zeros(1, kv_heads, max_len, head_dim, device=device, dtype=dtype) for _ in range(n_layers)]
+        self.max_len = max_len
+        self.length = 0
+
+
+class TPDecoder:
+    """One rank of a tensor-parallel decoder. `group` is a torch.distributed
+    process group (None for a single rank)."""
+
+    def __init__(self, hf_cfg, weights: dict, world: int = 1, rank: int = 0, group=None, device="cuda"):
+        self.cfg = hf_cfg
+        self.world, self.rank, self.group = world, rank, group
+        self.device = torch.device(device)
+        self.H = hf_cfg.hidden_size
+        self.hd = getattr(hf_cfg, "head_dim", None) or self.H // hf_cfg.num_attention_heads
+        self.nh = hf_cfg.num_attention_heads // world
+        self.nkv = hf_cfg.num_key_value_heads // world
+        if hf_cfg.num_attention_heads % world or hf_cfg.num_key_value_heads % world:
+            raise ValueError("attention heads do not divide across %d ranks" % world)
+        self.eps = hf_cfg.rms_norm_eps
+        self.n_layers = hf_cfg.num_hidden_layers
+        self.qk_norm = "model.layers.0.self_attn.q_norm.weight" in weights
+        self.vocab = hf_cfg.vocab_size
+        self.w = weights  # key -> tensor (shard) or a callable returning it
+        rp = getattr(hf_cfg, "rope_parameters", None) or {}
+        theta = rp.get("rope_theta", getattr(hf_cfg, "rope_theta", 10000.0))
+        self.inv_freq = 1.0 / (theta ** (torch.arange(0, self.hd, 2, dtype=torch.int64).to(
+            device=self.device, dtype=torch.float) / self.hd))
+
+    # -- weights -----------------------------------------------------------
+    def weight(self, key: str) -> torch.Tensor:
+        w = self.w[key]
+        return w() if callable(w) else w
+
+    # -- collectives ----------------------------------------------------------
+    def _all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if self.world > 1:
+            torch.distributed.all_reduce(x, group=self.group)
+        return x
+
+    def _all_gather_last(self, x: torch.Tensor) -> torch.Tensor:
+        if self.world == 1:
+            return x
+        parts = [torch.empty_like(x) for _ in range(self.world)]
+        torch.distributed.all_gather(parts, x.contiguous(), group=self.group)
+        return torch.cat(parts, dim=-1)
+
+    # -- forward -------------------------------------------------------------
+    def _rope(self, positions: torch.Tensor, dtype):
+        freqs = positions[:, None].float() * self.inv_freq[None, :]
+        emb = torch.cat((freqs, freqs), dim=-1)
+        return emb.cos().to(dtype), emb.sin().to(dtype)
+
+    def layer_weights(self, i: int) -> dict:
+        """Hook point: the compressed-resident subclass decodes here."""
+        p = "model.layers.%d." % i
+        names = ["input_layernorm.weight", "post_attention_layernorm.weight", "self_attn.q_proj.weight",
+                 "self_attn.k_proj.weight", "self_attn.v_proj.weight", "self_attn.o_proj.weight",
+                 "mlp.gate_proj.weight", "mlp.up_proj.weight", "mlp.down_proj.weight"]
+        if self.qk_norm:
+            names += ["self_attn.q_norm.weight", "self_attn.k_norm.weight"]
+        return {n: self.weight(p + n) for n in names}
+
+    def _layer(self, i: int, x: torch.Tensor, cos, sin, cache: KVCache | None, start: int) -> torch.Tensor:
+        W = self.layer_weights(i)
+        T = x.shape[0]
+        h = _rms_norm(x, W["input_layernorm.weight"], self.eps)
+        q = F.linear(h, W["self_attn.q_proj.weight"]).view(T, self.nh, self.hd)
+        k = F.linear(h, W["self_attn.k_proj.weight"]).view(T, self.nkv, self.hd)
+        v = F.linear(h, W["self_attn.v_proj.weight"]).view(T, self.nkv, self.hd)
+        if self.qk_norm:
+            q = _rms_norm(q, W["self_attn.q_norm.weight"], self.eps)
+            k = _rms_norm(k, W["self_attn.k_norm.weight"], self.eps)
+        q, k, v = q.transpose(0, 1)[None], k.transpose(0, 1)[None], v.transpose(0, 1)[None]
+        q = q * cos + _rotate_half(q) * sin
+        k = k * cos + _rotate_half(k) * sin
+        if cache is not None:
+            cache.k[i][:, :, start:start + T] = k
+            cache.v[i][:, :, start:start + T] = v
+            k = cache.k[i][:, :, :start + T]
+            v = cache.v[i][:, :, :start + T]
+        L = k.shape[2]
+        if T == 1:
+            mask = None
+        else:
+            qpos = torch.arange(start, start + T, device=x.device)[:, None]
+            mask = torch.arange(L, device=x.device)[None, :] <= qpos
+        a = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=self.hd ** -0.5,
+                                           enable_gqa=self.nh != self.nkv)
+        a = a[0].transpose(0, 1).reshape(T, self.nh * self.hd)
+        x = x + self._all_reduce(F.linear(a, W["self_attn.o_proj.weight"]))
+        h = _rms_norm(x, W["post_attention_layernorm.weight"], self.eps)
+        m = F.silu(F.linear(h, W["mlp.gate_proj.weight"])) * F.linear(h, W["mlp.up_proj.weight"])
+        return x + self._all_reduce(F.linear(m, W["mlp.down_proj.weight"]))
+
+    def embed(self, ids: torch.Tensor) -> torch.Tensor:
+        e = self.w["model.embed_tokens.weight"]
+        if callable(e):
+            return e(ids)
+        return F.embedding(ids, e)
+
+    @torch.no_grad()
+    def forward(self, input_ids: torch.Tensor, cache: KVCache | None = None) -> torch.Tensor:
+        """Logits [T, vocab] for the T tokens of `input_ids` (batch 1),
+        appended to `cache` when given."""
+        ids = input_ids.reshape(-1).to(self.device)
+        start = cache.length if cache is not None else 0
+        T = ids.shape[0]
+        x = self.embed(ids)
+        pos = torch.arange(start, start + T, device=self.device)
+        cos, sin = self._rope(pos, x.dtype)
+        for i in range(self.n_layers):
+            x = self._layer(i, x, cos, sin, cache, start)
+        if cache is not None:
+            cache.length = start + T
+        x = _rms_norm(x, self.weight("model.norm.weight"), self.eps)
+        head = self.w.get("lm_head.weight", None)
+        logits = F.linear(x, self.weight("lm_head.weight") if head is not None else self.full_embed_shard())
+        return self._all_gather_last(logits)
+
+    def full_embed_shard(self) -> torch.Tensor:
+        """Tied head: this rank's vocab rows of the (replicated) embedding."""
+        e = self.weight("model.embed_tokens.weight")
+        v0, v1 = _split(self.vocab, self.world, self.rank)
+        return e[v0:v1]
+
+    @torch.no_grad()
+    def generate_greedy(self, input_ids: torch.Tensor, max_new_tokens: int, max_len: int | None = None):
+        ids = input_ids.reshape(1, -1)
+        max_len = max_len or ids.shape[1] + max_new_tokens
+        cache = KVCache(self.n_layers, self.nkv, self.hd, max_len, self.device)
+        seq = ids.to(self.device)
+        step = seq
+        for _ in range(max_new_tokens):
+            logits = self.forward(step, cache)
+            nxt = logits[-1:].argmax(-1).reshape(1, 1)
+            seq = torch.cat([seq, nxt], 1)
+            step = nxt
+        return seq
+
+
+class CompressedTPDecoder(TPDecoder):
+    """TP decoder whose projection shards stay compressed in HBM; each
+    layer's seven shards are decoded by one batched launch per forward."""
+
+    def __init__(self, hf_cfg, weights: dict, streams: dict, world=1, rank=0, group=None, device="cuda"):
+        super().__init__(hf_cfg, weights, world, rank, group, device)
+        self.dev = _device.cuda_device(device)
+        self.decoder = LayerDecoder(self.dev)
+        self.resident = {k: (upload_layer(s.layer, self.dev), s) for k, s in streams.items()}
+        self.by_layer = [[(k, r, s) for k, (r, s) in self.resident.items() if k.startswith("model.layers.%d." % i)]
+                         for i in range(self.n_layers)]
+        self.layer_keys = [[k for k, v in self.w.items() if v is not None and k.startswith("model.layers.%d." % i)]
+                           for i in range(self.n_layers)]
+
+    def layer_weights(self, i: int) -> dict:
+        p = "model.layers.%d." % i
+        W = {}
+        todo = self.by_layer[i]
+        outs = [torch.empty(res.shape, dtype=torch.bfloat16, device=self.dev) for _, res, _ in todo]
+        self.decoder.decode([res for _, res, _ in todo], outs)
+        for (key, res, ss), o in zip(todo, outs):
+            W[key[len(p):]] = o.view(ss.rows, ss.cols_decoded) if ss.exact else ss.finish(o)
+        # norms, and projections the store kept raw (incompressible), are resident as-is
+        for key in self.layer_keys[i]:
+            if key[len(p):] not in W:
+                W[key[len(p):]] = self.w[key]
+        return W
+
+
+def load_tp_decoder(store_dir, hf_cfg, world: int = 1, rank: int = 0, group=None, device="cuda",
+                    resident: str = "decoded") -> TPDecoder:
+    """Builds rank `rank`'s decoder from a compressed store: projection
+    shards gathered on the host and either decoded once (resident="decoded")
+    or kept compressed in HBM (resident="compressed"); norms and the
+    embedding replicated; the head split by vocabulary."""
+    from .compressed_store import decompress_layer_gpu
+    store = pathlib.Path(store_dir)
+    manifest = json.loads((store / "manifest.json").read_text())
+    dev = _device.cuda_device(device)
+    weights: dict = {}
+    streams: dict = {}
+    with BinaryWeightReader(store / "weights.bin") as reader:
+        for key, meta in manifest["tensors"].items():
+            blobs = {n: reader.read(ref) for n, ref in meta["blobs"].items()}
+            if meta.get("row_gather"):
+                # untied embedding: replicated rows read on demand
+                from .streaming_engine import _raw_tensor
+                table = _raw_tensor(meta, blobs["raw"]).reshape(meta["shape"]).to(dev)
+                weights[key] = table
+                continue
+            if not meta["compressed"]:
+                # stored raw (incompressible): shard by slicing
+                from .streaming_engine import _raw_tensor
+                t = _raw_tensor(meta, blobs["raw"]).reshape(meta["shape"])
+                kind = shard_kind(key)
+                if kind == "col":
+                    r0, r1 = _split(t.shape[0], world, rank)
+                    t = t[r0:r1]
+                elif kind == "row":
+                    c0, c1 = _split(t.shape[1], world, rank)
+                    t = t[:, c0:c1]
+                weights[key] = t.contiguous().to(dev)
+                continue
+            from .streaming_engine import _encoded_from_arrays
+            layer = _encoded_from_arrays(meta, blobs)
+            kind = shard_kind(key)
+            if kind == "rep":
+                weights[key] = decompress_layer_gpu(layer, device=dev)
+                continue
+            ss = shard_stream(layer, kind, world, rank)
+            if resident == "compressed" and key.startswith("model.layers."):
+                streams[key] = ss
+                weights[key] = None
+                continue
+            weights[key] = ss.finish(decompress_layer_gpu(ss.layer, device=dev))
+    if "lm_head.weight" not in weights and not getattr(hf_cfg, "tie_word_embeddings", False):
+        raise RuntimeError("store has no lm_head.weight and the model is not tied")
+    if resident == "compressed":
+        return CompressedTPDecoder(hf_cfg, weights, streams, world, rank, group, dev)
+    return TPDecoder(hf_cfg, weights, world, rank, group, dev)

@@ -1,0 +1,108 @@
+"""Tensor-parallel decoder on the GPU, loaded from a compressed store: one
+GPU (decoded and compressed-resident shards) and, when two GPUs are
+present, two NCCL ranks -- logits within BF16 tolerance of a plain
+transformers forward, greedy tokens equal where the top-2 margin is clear."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+from test_streaming_engine_gpu import _store, _tiny
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref_greedy(model, ids, n):
+    seq = ids
+    margins = []
+    with torch.no_grad():
+        for _ in range(n):
+            lg = model(input_ids=seq).logits[0, -1].float()
+            top = torch.topk(lg, 2).values
+            margins.append(float(top[0] - top[1]))
+            seq = torch.cat([seq, lg.argmax().reshape(1, 1)], 1)
+    return seq, margins
+
+
+def _check_greedy(seq, ref_seq, margins, n_prompt):
+    for t, mg in enumerate(margins):
+        if mg > 0.05:
+            assert int(seq[0, n_prompt + t]) == int(ref_seq[0, n_prompt + t])
+        else:
+            break  # after a near-tie the continuations may legitimately differ
+
+
+@pytest.fixture(scope="module")
+def stores(tmp_path_factory):
+    from afterimage_b200.runtime.streaming_engine import write_store
+    tmp = tmp_path_factory.mktemp("tp")
+    cfg, model = _tiny(tie=False, seed=21, layers=2)
+    snap, store, _ = _store(tmp, cfg, model, "ref")  # reference chunking (256)
+    tp_store = tmp / "tp_ready"
+    write_store(((k, v.contiguous()) for k, v in model.state_dict().items()), tp_store, tied=False,
+                tp_row_chunks=4)
+    return cfg, model, store, tp_store
+
+
+@pytest.mark.parametrize("resident", ["decoded", "compressed"])
+@pytest.mark.parametrize("which", ["ref", "tp_ready"])
+def test_tp_single_gpu_matches_transformers(stores, resident, which):
+    from afterimage_b200.runtime.tp_decoder import load_tp_decoder
+    cfg, model, store, tp_store = stores
+    dec = load_tp_decoder(store if which == "ref" else tp_store, cfg, 1, 0, None, "cuda", resident=resident)
+    model = model.to("cuda")
+    ids = torch.randint(0, cfg.vocab_size, (1, 11), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits[0].float()
+    got = dec.forward(ids).float()
+    assert torch.allclose(got, ref, atol=2e-2, rtol=0), float((got - ref).abs().max())
+    seq = dec.generate_greedy(ids, 5)
+    ref_seq, margins = _ref_greedy(model, ids, 5)
+    _check_greedy(seq, ref_seq, margins, 11)
+
+
+def _rank_main(rank, world, port, tp_store, cfg_dict, ids, q):
+    from transformers import Qwen3Config
+    from afterimage_b200.runtime.tp_decoder import load_tp_decoder
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    torch.distributed.init_process_group("nccl", rank=rank, world_size=world,
+                                         timeout=datetime.timedelta(seconds=120),
+                                         device_id=torch.device("cuda", rank))
+    try:
+        cfg = Qwen3Config(**cfg_dict)
+        dec = load_tp_decoder(tp_store, cfg, world, rank, None, "cuda:%d" % rank, resident="compressed")
+        logits = dec.forward(ids.to("cuda:%d" % rank)).float().cpu().numpy()
+        seq = dec.generate_greedy(ids.to("cuda:%d" % rank), 5).cpu().numpy()
+        q.put((rank, logits, seq))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp_two_gpus_nccl_matches_transformers(stores):
+    cfg, model, store, tp_store = stores
+    ids = torch.randint(0, cfg.vocab_size, (1, 11))
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tp_store), cfg.to_dict(), ids, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = sorted([q.get(timeout=300) for _ in range(2)], key=lambda g: g[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    model = model.to("cuda:0")
+    with torch.no_grad():
+        ref = model(input_ids=ids.to("cuda:0")).logits[0].float().cpu()
+    for rank, logits, seq in got:
+        logits = torch.from_numpy(logits)
+        assert torch.allclose(logits, ref, atol=3e-2, rtol=0), float((logits - ref).abs().max())
+    ref_seq, margins = _ref_greedy(model, ids.to("cuda:0"), 5)
+    _check_greedy(torch.from_numpy(got[0][2]), ref_seq.cpu(), margins, 11)
