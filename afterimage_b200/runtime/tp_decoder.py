@@ -31,11 +31,13 @@ import numpy as np
 import torch
 import torch.nn.functional as F
 
+from .. import _lib
 from . import _device
 from .binstore import BinaryWeightReader
 from .compressed_store import CompressedLayer
 from .huffman_chunked import ChunkedEncoded
-from .layer_decode import LayerDecoder, upload_layer
+from .gpu_decode_v2 import prepare_decode_tables
+from .layer_decode import LayerDecoder
 
 COL_PARALLEL = ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj")
 ROW_PARALLEL = ("o_proj", "down_proj")
@@ -278,9 +280,12 @@ class TPDecoder:
         if cache is not None:
             cache.length = start + T
         x = _rms_norm(x, self.weight("model.norm.weight"), self.eps)
+        return self._all_gather_last(self.head_logits(x))
+
+    def head_logits(self, x: torch.Tensor) -> torch.Tensor:
+        """This rank's vocab shard of the logits."""
         head = self.w.get("lm_head.weight", None)
-        logits = F.linear(x, self.weight("lm_head.weight") if head is not None else self.full_embed_shard())
-        return self._all_gather_last(logits)
+        return F.linear(x, self.weight("lm_head.weight") if head is not None else self.full_embed_shard())
 
     def full_embed_shard(self) -> torch.Tensor:
         """Tied head: this rank's vocab rows of the (replicated) embedding."""
@@ -303,55 +308,337 @@ class TPDecoder:
         return seq
 
 
-class CompressedTPDecoder(TPDecoder):
-    """TP decoder whose projection shards stay compressed in HBM; each
-    layer's seven shards are decoded by one batched launch per forward."""
+_ALIGN = 256
 
-    def __init__(self, hf_cfg, weights: dict, streams: dict, world=1, rank=0, group=None, device="cuda"):
+
+class HostArena:
+    """One page-locked host allocation of exactly `nbytes` (an anonymous
+    mapping registered with the CUDA driver), so that uploads from it are
+    asynchronous DMA copies; torch's pinned allocator would round every
+    block up to a power of two."""
+
+    def __init__(self, nbytes: int):
+        import mmap
+        self.nbytes = max(int(nbytes), 4096)
+        self._map = mmap.mmap(-1, self.nbytes)
+        self.array = np.frombuffer(self._map, dtype=np.uint8)
+        err = torch._C._cudart.cudaHostRegister(self.array.ctypes.data, self.nbytes, 0)
+        if int(err) != 0:
+            raise RuntimeError("cudaHostRegister of %d bytes failed (%s)" % (self.nbytes, err))
+        self.tensor = torch.from_numpy(self.array)
+
+    def close(self) -> None:
+        if self._map is not None:
+            torch._C._cudart.cudaHostUnregister(self.array.ctypes.data)
+            self.tensor = None
+            self.array = None
+            self._map = None  # released with the last view
+
+
+@dataclasses.dataclass
+class _Seg:
+    """Where one shard's stream sits inside its layer's byte image."""
+    key: str
+    ss: ShardStream
+    tables: object
+    packed_off: int
+    packed_n: int
+    packed_cap: int
+    offs_off: int
+    nbs_off: int
+    n_chunks: int
+    sm_off: int
+
+
+def _up(x: int) -> int:
+    return (x + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+def _layer_layout(streams: list[tuple[str, ShardStream]], tables: dict) -> tuple[list[_Seg], int]:
+    segs, pos = [], 0
+    for key, ss in streams:
+        enc = ss.layer.encoded
+        pn = int(np.asarray(enc.packed).shape[0])
+        cap = max(16, (pn + 15) // 16 * 16)
+        nc = int(enc.n_chunks)
+        seg = _Seg(key, ss, tables[key], pos, pn, cap, 0, 0, nc, 0)
+        pos = _up(pos + cap)
+        seg.offs_off = pos
+        pos = _up(pos + 4 * max(nc, 1))
+        seg.nbs_off = pos
+        pos = _up(pos + 4 * max(nc, 1))
+        seg.sm_off = pos
+        pos = _up(pos + int(ss.layer.sign_mantissa.numel()))
+        segs.append(seg)
+    return segs, pos
+
+
+def _fill_image(dst: np.ndarray, segs: list[_Seg]) -> None:
+    for g in segs:
+        enc = g.ss.layer.encoded
+        dst[g.packed_off:g.packed_off + g.packed_n] = np.asarray(enc.packed)
+        dst[g.packed_off + g.packed_n:g.packed_off + g.packed_cap] = 0
+        dst[g.offs_off:g.offs_off + 4 * g.n_chunks] = np.asarray(enc.chunk_offsets, dtype=np.int32).view(np.uint8)
+        dst[g.nbs_off:g.nbs_off + 4 * g.n_chunks] = np.asarray(enc.chunk_nbytes, dtype=np.int32).view(np.uint8)
+        sm = g.ss.layer.sign_mantissa.reshape(-1).numpy()
+        dst[g.sm_off:g.sm_off + sm.shape[0]] = sm
+
+
+class CompressedTPDecoder(TPDecoder):
+    """TP decoder whose projection shards stay compressed; each layer's
+    shards are decoded by one batched launch per forward, straight into
+    the [rows, cols] weights (the element range skips a column shard's
+    partial leading chunk).
+
+    Each layer's shards form one byte image: per tensor the packed stream
+    (16-byte padded), int32 chunk offsets and byte counts, and the
+    sign/mantissa bytes, each 256-byte aligned.
+      * mode="compressed": every image resident in HBM (uploaded once).
+      * mode="streamed": images in page-locked host memory; `slots` device
+        buffers hold the next layers, filled by one copy per layer on a
+        copy stream that runs ahead of the compute stream (layer i+slots
+        uploads into layer i's buffer as soon as its decode has run), so
+        the PCIe transfer overlaps decode and projection.
+    The head (vocab rows of lm_head, or of a tied embedding) stays compressed
+    in HBM and is decoded `head_block_rows` rows at a time into one reused
+    buffer, so it never exists decoded in full. With `overlap`, layer i+1 is
+    decoded on a side stream while layer i's projections run."""
+
+    def __init__(self, hf_cfg, weights: dict, streams: dict, world=1, rank=0, group=None, device="cuda",
+                 mode: str = "compressed", slots: int = 2, head_block_rows: int = 16384, overlap: bool = False):
         super().__init__(hf_cfg, weights, world, rank, group, device)
+        if mode not in ("compressed", "streamed"):
+            raise ValueError("mode must be 'compressed' or 'streamed'")
         self.dev = _device.cuda_device(device)
+        self.mode = mode
         self.decoder = LayerDecoder(self.dev)
-        self.resident = {k: (upload_layer(s.layer, self.dev), s) for k, s in streams.items()}
-        self.by_layer = [[(k, r, s) for k, (r, s) in self.resident.items() if k.startswith("model.layers.%d." % i)]
-                         for i in range(self.n_layers)]
+        self.tables = {k: prepare_decode_tables(ss.layer.encoded, self.dev) for k, ss in streams.items()}
         self.layer_keys = [[k for k, v in self.w.items() if v is not None and k.startswith("model.layers.%d." % i)]
                            for i in range(self.n_layers)]
+        self.segs, sizes = [], []
+        for i in range(self.n_layers):
+            pre = "model.layers.%d." % i
+            segs, nb = _layer_layout([(k, ss) for k, ss in streams.items() if k.startswith(pre)], self.tables)
+            self.segs.append(segs)
+            sizes.append(nb)
+        head_key = "lm_head.weight" if "lm_head.weight" in streams else None
+        self.head = None
+        if head_key is not None:
+            hsegs, hn = _layer_layout([(head_key, streams[head_key])], self.tables)
+            img = np.zeros(hn, dtype=np.uint8)
+            _fill_image(img, hsegs)
+            self.head = (hsegs[0], torch.from_numpy(img).to(self.dev))
+            self.head_block_rows = max(1, int(head_block_rows))
+        self._desc_cache: dict = {}
+        self.overlap = bool(overlap)
+        self._dec_stream = torch.cuda.Stream(self.dev) if self.overlap else None
+        self._ahead: dict = {}
+        if mode == "compressed":
+            self.images = []
+            for i in range(self.n_layers):
+                img = np.zeros(max(sizes[i], 16), dtype=np.uint8)
+                _fill_image(img, self.segs[i])
+                self.images.append(torch.from_numpy(img).to(self.dev))
+        else:
+            offs = np.concatenate([[0], np.cumsum([_up(max(n, 16)) for n in sizes])]).astype(np.int64)
+            self.arena = HostArena(int(offs[-1]))
+            self.host = []
+            for i in range(self.n_layers):
+                view = self.arena.array[offs[i]:offs[i] + max(sizes[i], 16)]
+                _fill_image(view, self.segs[i])
+                self.host.append(self.arena.tensor[offs[i]:offs[i] + max(sizes[i], 16)])
+            cap = _up(max(max(sizes), 16))
+            self.slots = [torch.empty(cap, dtype=torch.uint8, device=self.dev) for _ in range(max(1, slots))]
+            self.copy_stream = torch.cuda.Stream(self.dev)
+            self._consumed = [None] * len(self.slots)
+            self._pending: list = []      # (layer, slot, upload-done event), in upload order
+            self._next_slot = 0
+            self.h2d_bytes = 0
+
+    # -- streamed pipeline ---------------------------------------------------------
+    def _issue_upload(self, layer: int) -> None:
+        slot = self._next_slot
+        self._next_slot = (slot + 1) % len(self.slots)
+        cs = self.copy_stream
+        if self._consumed[slot] is not None:
+            cs.wait_event(self._consumed[slot])
+        src = self.host[layer]
+        with torch.cuda.stream(cs):
+            self.slots[slot][:src.numel()].copy_(src, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(cs)
+        self.h2d_bytes += src.numel()
+        self._pending.append((layer, slot, ev))
+
+    def _take_image(self, i: int) -> tuple[torch.Tensor, int, object]:
+        """(device image holding layer i, slot id or -1, event to wait on)."""
+        if self.mode == "compressed":
+            return self.images[i], -1, None
+        if not self._pending or self._pending[0][0] != i:
+            # out of step (first use, or a forward that stopped early): restart the ring at layer i
+            self.copy_stream.synchronize()
+            self._pending.clear()
+            for j in range(len(self.slots)):
+                self._issue_upload((i + j) % self.n_layers)
+        layer, slot, ev = self._pending.pop(0)
+        return self.slots[slot], slot, ev
+
+    def _release_image(self, slot: int, stream) -> None:
+        if slot < 0:
+            return
+        done = torch.cuda.Event()
+        done.record(stream)
+        self._consumed[slot] = done
+        last = self._pending[-1][0] if self._pending else None
+        nxt = ((last if last is not None else -1) + 1) % self.n_layers
+        self._issue_upload(nxt)
+
+    # -- decode ----------------------------------------------------------------
+    def _descs(self, i: int, segs: list[_Seg], base: torch.Tensor, tag, outs: list[torch.Tensor]):
+        key = (i, tag, tuple(o.data_ptr() for o in outs))
+        d = self._desc_cache.get(key)
+        if d is None:
+            d = (_lib.StreamDesc * len(segs))()
+            for j, (g, o) in enumerate(zip(segs, outs)):
+                ss = g.ss
+                ds = _device.DeviceStream(packed=base[g.packed_off:g.packed_off + g.packed_cap], nbytes=g.packed_n,
+                                          capacity=g.packed_cap, offset_base=0,
+                                          offsets=base[g.offs_off:g.offs_off + 4 * max(g.n_chunks, 1)].view(torch.int32),
+                                          chunk_nbytes=base[g.nbs_off:g.nbs_off + 4 * max(g.n_chunks, 1)].view(torch.int32),
+                                          chunk_base=0)
+                e0 = ss.elem_lo
+                e1 = e0 + ss.rows * ss.cols_decoded
+                d[j] = _device.make_desc(ds, g.tables, ss.layer.encoded, e0, e1, o, base[g.sm_off + e0:])
+            if len(self._desc_cache) > 8 * self.n_layers + 16:
+                self._desc_cache.clear()
+            self._desc_cache[key] = d
+        return d
+
+    def _decode_layer(self, i: int, stream) -> dict:
+        """Enqueues layer i's decode on `stream`; returns name -> weight."""
+        p = "model.layers.%d." % i
+        segs = self.segs[i]
+        W = {}
+        with torch.cuda.stream(stream):
+            image, slot, ev = self._take_image(i)
+            if ev is not None:
+                stream.wait_event(ev)
+            outs = [torch.empty(g.ss.rows, g.ss.cols_decoded, dtype=torch.bfloat16, device=self.dev) for g in segs]
+            if segs:
+                self.decoder.launch(self._descs(i, segs, image, slot, outs), len(segs))
+            self._release_image(slot, stream)
+            for g, o in zip(segs, outs):
+                ss = g.ss
+                W[g.key[len(p):]] = o if (ss.col_lo == 0 and ss.cols == ss.cols_decoded) else \
+                    o[:, ss.col_lo:ss.col_lo + ss.cols].contiguous()
+        return W
 
     def layer_weights(self, i: int) -> dict:
+        compute = torch.cuda.current_stream(self.dev)
+        if not self.overlap:
+            W = self._decode_layer(i, compute)
+        else:
+            ds = self._dec_stream
+            if i not in self._ahead:
+                self._ahead[i] = (self._decode_layer(i, ds), self._event(ds))
+            W, ev = self._ahead.pop(i)
+            compute.wait_event(ev)
+            for t in W.values():
+                t.record_stream(compute)
+            # the next layer decodes on the side stream while this one's projections run
+            # (fresh outputs from the caching allocator: nothing on the compute stream to wait for)
+            nxt = i + 1
+            if nxt < self.n_layers:
+                self._ahead[nxt] = (self._decode_layer(nxt, ds), self._event(ds))
         p = "model.layers.%d." % i
-        W = {}
-        todo = self.by_layer[i]
-        outs = [torch.empty(res.shape, dtype=torch.bfloat16, device=self.dev) for _, res, _ in todo]
-        self.decoder.decode([res for _, res, _ in todo], outs)
-        for (key, res, ss), o in zip(todo, outs):
-            W[key[len(p):]] = o.view(ss.rows, ss.cols_decoded) if ss.exact else ss.finish(o)
         # norms, and projections the store kept raw (incompressible), are resident as-is
         for key in self.layer_keys[i]:
             if key[len(p):] not in W:
                 W[key[len(p):]] = self.w[key]
         return W
 
+    @staticmethod
+    def _event(stream):
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        return ev
+
+    def head_logits(self, x: torch.Tensor) -> torch.Tensor:
+        if self.head is None:
+            return super().head_logits(x)
+        g, image = self.head
+        ss = g.ss
+        rows, cols = ss.rows, ss.cols
+        out = torch.empty(x.shape[0], rows, dtype=x.dtype, device=self.dev)
+        blk = self.head_block_rows
+        buf = torch.empty(min(blk, rows) * ss.cols_decoded, dtype=torch.bfloat16, device=self.dev)
+        for r0 in range(0, rows, blk):
+            r1 = min(rows, r0 + blk)
+            w = buf[:(r1 - r0) * ss.cols_decoded]
+            e0 = ss.elem_lo + r0 * ss.cols_decoded
+            ds = _device.DeviceStream(packed=image[g.packed_off:g.packed_off + g.packed_cap], nbytes=g.packed_n,
+                                      capacity=g.packed_cap, offset_base=0,
+                                      offsets=image[g.offs_off:g.offs_off + 4 * max(g.n_chunks, 1)].view(torch.int32),
+                                      chunk_nbytes=image[g.nbs_off:g.nbs_off + 4 * max(g.n_chunks, 1)].view(torch.int32),
+                                      chunk_base=0)
+            d = (_lib.StreamDesc * 1)()
+            d[0] = _device.make_desc(ds, g.tables, ss.layer.encoded, e0, e0 + w.numel(), w, image[g.sm_off + e0:])
+            self.decoder.launch(d, 1)
+            wv = w.view(r1 - r0, ss.cols_decoded)[:, ss.col_lo:ss.col_lo + cols]
+            out[:, r0:r1] = F.linear(x, wv)
+        return out
+
+    def close(self) -> None:
+        if self.mode == "streamed":
+            self.copy_stream.synchronize()
+            torch.cuda.synchronize(self.dev)
+            self.slots = []
+            self.host = []
+            self.arena.close()
+
+
+class HostRows:
+    """Embedding rows gathered on the host from a page-locked table and
+    uploaded per call (the row-gather embedding; the table never occupies
+    device memory)."""
+
+    def __init__(self, table: torch.Tensor, device):
+        self.table = table.pin_memory() if torch.cuda.is_available() else table
+        self.device = device
+
+    def __call__(self, ids: torch.Tensor) -> torch.Tensor:
+        rows = self.table.index_select(0, ids.to("cpu"))
+        return rows.to(self.device, non_blocking=False)
+
 
 def load_tp_decoder(store_dir, hf_cfg, world: int = 1, rank: int = 0, group=None, device="cuda",
-                    resident: str = "decoded") -> TPDecoder:
-    """Builds rank `rank`'s decoder from a compressed store: projection
-    shards gathered on the host and either decoded once (resident="decoded")
-    or kept compressed in HBM (resident="compressed"); norms and the
-    embedding replicated; the head split by vocabulary."""
+                    resident: str = "decoded", **kw) -> TPDecoder:
+    """Builds rank `rank`'s decoder from a compressed store. Projection
+    shards are cut from the chunk streams on the host and then
+      resident="decoded":    decoded once into BF16 shards in HBM;
+      resident="compressed": kept compressed in HBM, decoded per forward;
+      resident="streamed":   kept compressed in page-locked host memory and
+                             copied to the device one layer at a time.
+    Norms are replicated; the head is split by vocabulary (kept compressed
+    unless decoded); an untied row-gather embedding stays in host memory
+    when streamed. Extra keywords go to CompressedTPDecoder."""
     from .compressed_store import decompress_layer_gpu
+    if resident not in ("decoded", "compressed", "streamed"):
+        raise ValueError("resident must be 'decoded', 'compressed' or 'streamed'")
     store = pathlib.Path(store_dir)
     manifest = json.loads((store / "manifest.json").read_text())
     dev = _device.cuda_device(device)
     weights: dict = {}
     streams: dict = {}
+    keep_compressed = resident in ("compressed", "streamed")
     with BinaryWeightReader(store / "weights.bin") as reader:
         for key, meta in manifest["tensors"].items():
             blobs = {n: reader.read(ref) for n, ref in meta["blobs"].items()}
             if meta.get("row_gather"):
-                # untied embedding: replicated rows read on demand
+                # untied embedding stored raw: replicated rows
                 from .streaming_engine import _raw_tensor
-                table = _raw_tensor(meta, blobs["raw"]).reshape(meta["shape"]).to(dev)
-                weights[key] = table
+                table = _raw_tensor(meta, blobs["raw"]).reshape(meta["shape"])
+                weights[key] = HostRows(table, dev) if resident == "streamed" else table.to(dev)
                 continue
             if not meta["compressed"]:
                 # stored raw (incompressible): shard by slicing
@@ -373,13 +660,14 @@ def load_tp_decoder(store_dir, hf_cfg, world: int = 1, rank: int = 0, group=None
                 weights[key] = decompress_layer_gpu(layer, device=dev)
                 continue
             ss = shard_stream(layer, kind, world, rank)
-            if resident == "compressed" and key.startswith("model.layers."):
+            if keep_compressed and (key.startswith("model.layers.") or key == "lm_head.weight"):
                 streams[key] = ss
                 weights[key] = None
                 continue
             weights[key] = ss.finish(decompress_layer_gpu(ss.layer, device=dev))
     if "lm_head.weight" not in weights and not getattr(hf_cfg, "tie_word_embeddings", False):
         raise RuntimeError("store has no lm_head.weight and the model is not tied")
-    if resident == "compressed":
-        return CompressedTPDecoder(hf_cfg, weights, streams, world, rank, group, dev)
+    if keep_compressed:
+        return CompressedTPDecoder(hf_cfg, weights, streams, world, rank, group, dev,
+                                   mode="streamed" if resident == "streamed" else "compressed", **kw)
     return TPDecoder(hf_cfg, weights, world, rank, group, dev)

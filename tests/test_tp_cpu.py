@@ -11,7 +11,9 @@ import torch.multiprocessing as mp
 
 from oracle import oracle as O
 from afterimage_b200.runtime.compressed_store import compress_layer
-from afterimage_b200.runtime.tp_decoder import TPDecoder, shard_kind, shard_stream, _split
+from afterimage_b200.runtime.huffman_chunked import ChunkedEncoded
+from afterimage_b200.runtime.tp_decoder import (TPDecoder, _fill_image, _layer_layout, shard_kind, shard_stream,
+                                                _split)
 
 
 @pytest.mark.parametrize("kind", ["col", "row"])
@@ -35,6 +37,40 @@ def test_shard_stream_is_bit_exact(kind, world, cs, cols):
     assert np.array_equal(dec, want)
     if kind == "row" and cols % cs == 0 and (cols // world) % cs == 0:
         assert ss.cols == ss.cols_decoded  # TP-ready chunking: whole chunks, no over-decode
+
+
+def test_layer_image_layout_round_trips():
+    """A layer's byte image (the unit a streamed rank copies per layer)
+    holds each shard's stream, offsets, byte counts and sign/mantissa at
+    256-byte aligned offsets; streams read back from it decode bit-exactly."""
+    g = torch.Generator().manual_seed(5)
+    shapes = {"q": (96, 640), "o": (64, 320), "d": (40, 1000)}
+    streams, want = [], {}
+    for name, (r, c) in shapes.items():
+        W = (torch.randn(r, c, generator=g) * 0.02).to(torch.bfloat16)
+        kind = "row" if name in ("o", "d") else "col"
+        ss = shard_stream(compress_layer(W, chunk_size=256 if name != "d" else 100), kind, 2, 1)
+        streams.append((name, ss))
+        want[name] = ss
+    segs, nbytes = _layer_layout(streams, {k: None for k, _ in streams})
+    img = np.full(nbytes, 0xAB, dtype=np.uint8)
+    _fill_image(img, segs)
+    for seg in segs:
+        for off in (seg.packed_off, seg.offs_off, seg.nbs_off, seg.sm_off):
+            assert off % 256 == 0
+        assert seg.packed_cap % 16 == 0 and seg.packed_cap >= seg.packed_n + 0
+        enc = seg.ss.layer.encoded
+        packed = img[seg.packed_off:seg.packed_off + seg.packed_n]
+        offs = img[seg.offs_off:seg.offs_off + 4 * seg.n_chunks].view(np.int32)
+        nbs = img[seg.nbs_off:seg.nbs_off + 4 * seg.n_chunks].view(np.int32)
+        sm = img[seg.sm_off:seg.sm_off + seg.ss.layer.sign_mantissa.numel()]
+        assert np.all(img[seg.packed_off + seg.packed_n:seg.packed_off + seg.packed_cap] == 0)
+        back = ChunkedEncoded(packed=packed, chunk_offsets=offs, chunk_nbytes=nbs, sym_lut=enc.sym_lut,
+                              len_lut=enc.len_lut, max_bits=enc.max_bits, chunk_size=enc.chunk_size,
+                              n_symbols=enc.n_symbols, shape=enc.shape)
+        a = O.decompress(back, sm)
+        b = O.decompress(enc, seg.ss.layer.sign_mantissa.numpy())
+        assert np.array_equal(a, b)
 
 
 def test_shard_kinds():

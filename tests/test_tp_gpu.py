@@ -46,12 +46,15 @@ def stores(tmp_path_factory):
     return cfg, model, store, tp_store
 
 
-@pytest.mark.parametrize("resident", ["decoded", "compressed"])
+@pytest.mark.parametrize("resident,kw", [("decoded", {}), ("compressed", {}),
+                                         ("compressed", {"overlap": True, "head_block_rows": 500}),
+                                         ("streamed", {}), ("streamed", {"slots": 3, "overlap": True}),
+                                         ("streamed", {"slots": 1, "head_block_rows": 1536})])
 @pytest.mark.parametrize("which", ["ref", "tp_ready"])
-def test_tp_single_gpu_matches_transformers(stores, resident, which):
+def test_tp_single_gpu_matches_transformers(stores, resident, kw, which):
     from afterimage_b200.runtime.tp_decoder import load_tp_decoder
     cfg, model, store, tp_store = stores
-    dec = load_tp_decoder(store if which == "ref" else tp_store, cfg, 1, 0, None, "cuda", resident=resident)
+    dec = load_tp_decoder(store if which == "ref" else tp_store, cfg, 1, 0, None, "cuda", resident=resident, **kw)
     model = model.to("cuda")
     ids = torch.randint(0, cfg.vocab_size, (1, 11), device="cuda")
     with torch.no_grad():
@@ -61,9 +64,37 @@ def test_tp_single_gpu_matches_transformers(stores, resident, which):
     seq = dec.generate_greedy(ids, 5)
     ref_seq, margins = _ref_greedy(model, ids, 5)
     _check_greedy(seq, ref_seq, margins, 11)
+    if resident != "decoded":
+        _lib_status_clear()
+    if resident == "streamed":
+        assert dec.h2d_bytes > 0
+        dec.close()
 
 
-def _rank_main(rank, world, port, tp_store, cfg_dict, ids, q):
+def _lib_status_clear():
+    from afterimage_b200.runtime import _device
+    _device.check_status(torch.device("cuda", torch.cuda.current_device()))
+
+
+def test_tp_decoded_weights_bit_exact(stores):
+    """The compressed and streamed decoders produce exactly the weights of
+    the plain decode (every layer, every shard)."""
+    from afterimage_b200.runtime.tp_decoder import load_tp_decoder
+    cfg, model, store, tp_store = stores
+    sd = {k: v.to("cuda") for k, v in model.state_dict().items()}
+    for path in (store, tp_store):
+        for resident in ("compressed", "streamed"):
+            dec = load_tp_decoder(path, cfg, 1, 0, None, "cuda", resident=resident)
+            for rep in range(2):  # second pass: the streamed ring wraps around
+                for i in range(cfg.num_hidden_layers):
+                    W = dec.layer_weights(i)
+                    for name, w in W.items():
+                        assert torch.equal(w.view(torch.int16), sd["model.layers.%d.%s" % (i, name)].view(torch.int16))
+            if resident == "streamed":
+                dec.close()
+
+
+def _rank_main(rank, world, port, tp_store, cfg_dict, ids, q, resident):
     from transformers import Qwen3Config
     from afterimage_b200.runtime.tp_decoder import load_tp_decoder
     import datetime
@@ -74,16 +105,19 @@ def _rank_main(rank, world, port, tp_store, cfg_dict, ids, q):
                                          device_id=torch.device("cuda", rank))
     try:
         cfg = Qwen3Config(**cfg_dict)
-        dec = load_tp_decoder(tp_store, cfg, world, rank, None, "cuda:%d" % rank, resident="compressed")
+        dec = load_tp_decoder(tp_store, cfg, world, rank, None, "cuda:%d" % rank, resident=resident)
         logits = dec.forward(ids.to("cuda:%d" % rank)).float().cpu().numpy()
         seq = dec.generate_greedy(ids.to("cuda:%d" % rank), 5).cpu().numpy()
         q.put((rank, logits, seq))
+        if resident == "streamed":
+            dec.close()
     finally:
         torch.distributed.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp_two_gpus_nccl_matches_transformers(stores):
+@pytest.mark.parametrize("resident", ["compressed", "streamed"])
+def test_tp_two_gpus_nccl_matches_transformers(stores, resident):
     cfg, model, store, tp_store = stores
     ids = torch.randint(0, cfg.vocab_size, (1, 11))
     with socket.socket() as s:
@@ -91,7 +125,7 @@ def test_tp_two_gpus_nccl_matches_transformers(stores):
         port = s.getsockname()[1]
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tp_store), cfg.to_dict(), ids, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, str(tp_store), cfg.to_dict(), ids, q, resident)) for r in range(2)]
     for p in procs:
         p.start()
     got = sorted([q.get(timeout=300) for _ in range(2)], key=lambda g: g[0])
