@@ -170,6 +170,31 @@ def compress_one_tensor(key: str, W: torch.Tensor, cfg: EngineConfig, row_gather
             "comp_bytes": orig, "arrays": {"raw": W.to(torch.float32).numpy()}}
 
 
+def tp_chunk_size(in_features: int, parts: int, chunk_size: int) -> int:
+    """Chunk size for a row-parallel tensor split `parts` ways by columns:
+    a divisor of in_features/parts, so that every rank's column range is
+    whole chunks, chosen to keep chunks about as long as the default (a
+    kernel lane decodes one chunk: far fewer, longer chunks would leave the
+    GPU idle). Preferred: the multiple of 64 nearest to chunk_size within
+    [chunk_size/2, 2*chunk_size] (64-symbol multiples take the decoder's
+    vectorised merge); else the largest divisor <= chunk_size, if at least
+    a quarter of it. A segment no longer than chunk_size is one chunk.
+    Keeps `chunk_size` when the columns do not divide or nothing fits."""
+    if parts < 1 or in_features % parts:
+        return chunk_size
+    seg = in_features // parts
+    if seg % chunk_size == 0:
+        return chunk_size
+    if seg <= chunk_size:
+        return seg
+    divs = [d for d in range(1, min(seg, 2 * chunk_size) + 1) if seg % d == 0]
+    v64 = [d for d in divs if d % 64 == 0 and chunk_size // 2 <= d <= 2 * chunk_size]
+    if v64:
+        return min(v64, key=lambda d: (abs(d - chunk_size), -d))
+    best = max((d for d in divs if d <= chunk_size), default=1)
+    return best if 4 * best >= chunk_size else chunk_size
+
+
 def write_store(items, out_dir, config: EngineConfig | None = None, *, tied: bool, model_id: str = "",
                 revision: str | None = None, progress_every: int = 50, total: int | None = None,
                 tp_row_chunks: int | None = None) -> dict:
@@ -179,9 +204,10 @@ def write_store(items, out_dir, config: EngineConfig | None = None, *, tied: boo
     row-addressable; each tensor is released after it is written.
 
     tp_row_chunks=P makes the store tensor-parallel ready: the row-parallel
-    projections (o_proj, down_proj) use chunk_size = in_features / P, so
-    each of P (or any divisor of P) ranks owns whole chunks of every row.
-    The format is unchanged (chunk_size is per tensor)."""
+    projections (o_proj, down_proj) use a chunk_size that divides
+    in_features / P (`tp_chunk_size`), so each of P (or any divisor of P)
+    ranks owns whole chunks of every row. The format is unchanged
+    (chunk_size is per tensor)."""
     cfg = config or EngineConfig()
     out_dir = pathlib.Path(out_dir)
     out_dir.mkdir(parents=True, exist_ok=True)
@@ -193,9 +219,10 @@ def write_store(items, out_dir, config: EngineConfig | None = None, *, tied: boo
     with BinaryWeightWriter(out_dir / "weights.bin") as writer:
         for n, (key, W) in enumerate(items, 1):
             tcfg = cfg
-            if (tp_row_chunks and W.dim() == 2 and key.endswith(("o_proj.weight", "down_proj.weight"))
-                    and W.shape[1] % tp_row_chunks == 0):
-                tcfg = dataclasses.replace(cfg, chunk_size=W.shape[1] // tp_row_chunks)
+            if tp_row_chunks and W.dim() == 2 and key.endswith(("o_proj.weight", "down_proj.weight")):
+                cs = tp_chunk_size(int(W.shape[1]), int(tp_row_chunks), cfg.chunk_size)
+                if cs != cfg.chunk_size:
+                    tcfg = dataclasses.replace(cfg, chunk_size=cs)
             res = compress_one_tensor(key, W, tcfg, row_gather=(key == row_gather_key))
             del W
             entry = {"orig_bytes": res["orig_bytes"], "comp_bytes": res["comp_bytes"], "shape": res["shape"],

@@ -7,9 +7,10 @@ Sharding (one process per GPU, torch.distributed / NCCL):
     of chunk_size, decoded with the element-range decode;
   * row-parallel: o_proj, down_proj -- rank r owns input columns
     [r*in/P, (r+1)*in/P) of every row. A TP-ready store compresses these
-    tensors with chunk_size = in/P_max (write_store(tp_row_chunks=...)) so a
-    rank's columns are whole chunks, gathered into a flat stream; for other
-    chunk sizes the rank decodes the covering chunks of each row and slices;
+    tensors with a chunk_size dividing in/P_max (write_store(tp_row_chunks=...))
+    so a rank's columns are whole chunks, gathered into a flat stream; for
+    other chunk sizes the rank decodes the covering chunks of each row and
+    slices;
   * one all-reduce (sum) after o_proj and one after down_proj per layer,
     an all-gather of the vocab shards for logits.
 Heads divide across ranks (num_attention_heads and num_key_value_heads must
@@ -147,6 +148,65 @@ def shard_stream(layer: CompressedLayer, kind: str, world: int, rank: int) -> Sh
                                        shape=(n_dec,)), out_rows, dec_cols, lo, keep, elem_lo)
 
 
+def _mark(stream) -> torch.cuda.Event:
+    ev = torch.cuda.Event(enable_timing=True)
+    ev.record(stream)
+    return ev
+
+
+def _union(iv: list[tuple[float, float]]) -> list[tuple[float, float]]:
+    out: list[list[float]] = []
+    for a, b in sorted(iv):
+        if out and a <= out[-1][1]:
+            out[-1][1] = max(out[-1][1], b)
+        else:
+            out.append([a, b])
+    return [(a, b) for a, b in out]
+
+
+def _measure(iv: list[tuple[float, float]]) -> float:
+    return sum(b - a for a, b in iv)
+
+
+def _intersect(x: list[tuple[float, float]], y: list[tuple[float, float]]) -> float:
+    i = j = 0
+    tot = 0.0
+    while i < len(x) and j < len(y):
+        a, b = max(x[i][0], y[j][0]), min(x[i][1], y[j][1])
+        if b > a:
+            tot += b - a
+        if x[i][1] < y[j][1]:
+            i += 1
+        else:
+            j += 1
+    return tot
+
+
+def timeline_summary(timeline: list, base: torch.cuda.Event) -> dict:
+    """Busy time of each kind of work (decode launches, per-layer compute,
+    host->device layer copies) from CUDA events, and how much of it ran
+    concurrently: `decode_overlapped_ms` is decode time during which the
+    compute stream was also busy. Call after synchronising."""
+    iv: dict[str, list] = {}
+    rows = []
+    for kind, layer, a, b in timeline:
+        t0, t1 = base.elapsed_time(a), base.elapsed_time(b)
+        iv.setdefault(kind, []).append((t0, t1))
+        rows.append((kind, layer, round(t0, 4), round(t1, 4)))
+    u = {k: _union(v) for k, v in iv.items()}
+    span = (min(a for v in u.values() for a, _ in v), max(b for v in u.values() for _, b in v)) if u else (0, 0)
+    out = {"span_ms": round(span[1] - span[0], 4)}
+    for k, v in u.items():
+        out[k + "_busy_ms"] = round(_measure(v), 4)
+    if "decode" in u and "compute" in u:
+        out["decode_overlapped_ms"] = round(_intersect(u["decode"], u["compute"]), 4)
+    if "upload" in u:
+        busy = _union(u.get("decode", []) + u.get("compute", []))
+        out["upload_overlapped_ms"] = round(_intersect(u["upload"], busy), 4)
+    out["events"] = rows
+    return out
+
+
 def _rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     dt = x.dtype
     h = x.to(torch.float32)
@@ -169,6 +229,22 @@ class KVCache:
         self.length = 0
 
 
+class _StepState:
+    """Static buffers of the graphed single-token step."""
+
+    def __init__(self, dec: "TPDecoder", max_len: int):
+        dev = dec.device
+        self.max_len = max_len
+        self.cache = KVCache(dec.n_layers, dec.nkv, dec.hd, max_len, dev)
+        self.ids = torch.zeros(1, dtype=torch.long, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.long, device=dev)
+        self.step = torch.zeros(1, dtype=torch.long, device=dev)
+        self.tokens = torch.zeros(max_len, dtype=torch.long, device=dev)
+        self.arange = torch.arange(max_len, device=dev).view(1, max_len)
+        self.mask = torch.zeros(1, max_len, dtype=torch.bool, device=dev)  # [query, key]
+        self.graph = None
+
+
 class TPDecoder:
     """One rank of a tensor-parallel decoder. `group` is a torch.distributed
     process group (None for a single rank)."""
@@ -188,6 +264,8 @@ class TPDecoder:
         self.qk_norm = "model.layers.0.self_attn.q_norm.weight" in weights
         self.vocab = hf_cfg.vocab_size
         self.w = weights  # key -> tensor (shard) or a callable returning it
+        self.timeline = None  # a list to record (kind, layer, start event, end event) into
+        self._graph_state = None
         rp = getattr(hf_cfg, "rope_parameters", None) or {}
         theta = rp.get("rope_theta", getattr(hf_cfg, "rope_theta", 10000.0))
         self.inv_freq = 1.0 / (theta ** (torch.arange(0, self.hd, 2, dtype=torch.int64).to(
@@ -227,8 +305,18 @@ class TPDecoder:
             names += ["self_attn.q_norm.weight", "self_attn.k_norm.weight"]
         return {n: self.weight(p + n) for n in names}
 
-    def _layer(self, i: int, x: torch.Tensor, cos, sin, cache: KVCache | None, start: int) -> torch.Tensor:
+    def _layer(self, i: int, x: torch.Tensor, cos, sin, cache: KVCache | None, start: int,
+               static=None) -> torch.Tensor:
         W = self.layer_weights(i)
+        if self.timeline is None:
+            return self._layer_math(i, W, x, cos, sin, cache, start, static)
+        t0 = _mark(torch.cuda.current_stream(self.device))
+        x = self._layer_math(i, W, x, cos, sin, cache, start, static)
+        self.timeline.append(("compute", i, t0, _mark(torch.cuda.current_stream(self.device))))
+        return x
+
+    def _layer_math(self, i: int, W: dict, x: torch.Tensor, cos, sin, cache: KVCache | None,
+                    start: int, static=None) -> torch.Tensor:
         T = x.shape[0]
         h = _rms_norm(x, W["input_layernorm.weight"], self.eps)
         q = F.linear(h, W["self_attn.q_proj.weight"]).view(T, self.nh, self.hd)
@@ -240,13 +328,21 @@ class TPDecoder:
         q, k, v = q.transpose(0, 1)[None], k.transpose(0, 1)[None], v.transpose(0, 1)[None]
         q = q * cos + _rotate_half(q) * sin
         k = k * cos + _rotate_half(k) * sin
-        if cache is not None:
+        if static is not None:
+            # single-token step with static shapes (CUDA-graph safe): the position is a
+            # device tensor, attention runs over the whole cache with a length mask
+            cache.k[i].index_copy_(2, static.pos, k)
+            cache.v[i].index_copy_(2, static.pos, v)
+            k, v = cache.k[i], cache.v[i]
+        elif cache is not None:
             cache.k[i][:, :, start:start + T] = k
             cache.v[i][:, :, start:start + T] = v
             k = cache.k[i][:, :, :start + T]
             v = cache.v[i][:, :, :start + T]
         L = k.shape[2]
-        if T == 1:
+        if static is not None:
+            mask = static.mask
+        elif T == 1:
             mask = None
         else:
             qpos = torch.arange(start, start + T, device=x.device)[:, None]
@@ -272,6 +368,7 @@ class TPDecoder:
         ids = input_ids.reshape(-1).to(self.device)
         start = cache.length if cache is not None else 0
         T = ids.shape[0]
+        self.begin_forward()
         x = self.embed(ids)
         pos = torch.arange(start, start + T, device=self.device)
         cos, sin = self._rope(pos, x.dtype)
@@ -281,6 +378,80 @@ class TPDecoder:
             cache.length = start + T
         x = _rms_norm(x, self.weight("model.norm.weight"), self.eps)
         return self._all_gather_last(self.head_logits(x))
+
+    def begin_forward(self) -> None:
+        """Hook run at the start of every forward (stream forks)."""
+
+    def _static_step(self, st: "_StepState") -> None:
+        """One greedy single-token step on static buffers: embeds st.ids at
+        position st.pos, runs every layer, picks the argmax token, records it
+        at st.tokens[st.step] and advances ids/pos/step -- all on the
+        device, so the step can be captured and replayed as a CUDA graph."""
+        self.begin_forward()
+        x = F.embedding(st.ids, self.weight("model.embed_tokens.weight"))
+        cos, sin = self._rope(st.pos, x.dtype)
+        torch.le(st.arange, st.pos, out=st.mask)
+        for i in range(self.n_layers):
+            x = self._layer(i, x, cos, sin, st.cache, 0, static=st)
+        x = _rms_norm(x, self.weight("model.norm.weight"), self.eps)
+        logits = self._all_gather_last(self.head_logits(x))
+        nxt = logits[-1].argmax(-1, keepdim=True)
+        st.tokens.index_copy_(0, st.step, nxt)
+        st.ids.copy_(nxt)
+        st.pos.add_(1)
+        st.step.add_(1)
+
+    @torch.no_grad()
+    def generate_greedy_graphed(self, input_ids: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
+        """Greedy decoding with the single-token step captured once as a CUDA
+        graph (decode launches, projections, all-reduces, argmax and the
+        position update) and replayed per token; the prompt runs eagerly.
+        The embedding must be on the device."""
+        if callable(self.w.get("model.embed_tokens.weight")) or getattr(self, "mode", None) == "streamed":
+            raise ValueError("graphed generation needs device-resident weights and embedding "
+                             "(resident='decoded' or 'compressed')")
+        ids = input_ids.reshape(1, -1).to(self.device)
+        P = ids.shape[1]
+        if max_new_tokens < 1:
+            return ids
+        st = self._graph_state
+        if st is None or st.max_len < P + max_new_tokens:
+            self.release_graphs()
+            st = _StepState(self, max(128, P + max_new_tokens))
+            self._graph_state = st
+        st.cache.length = 0
+        logits = self.forward(ids, st.cache)
+        first = logits[-1:].argmax(-1).reshape(1)
+        if max_new_tokens == 1:
+            return torch.cat([ids, first.reshape(1, 1)], 1)
+        st.ids.copy_(first)
+        st.pos.fill_(P)
+        st.step.zero_()
+        todo = max_new_tokens - 1
+        if st.graph is None:
+            # one real step eagerly on a side stream (allocator pools, library and NCCL state), then capture
+            cur = torch.cuda.current_stream(self.device)
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(cur)
+            with torch.cuda.stream(side):
+                self._static_step(st)
+            cur.wait_stream(side)
+            torch.cuda.synchronize(self.device)
+            todo -= 1
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self._static_step(st)
+            st.graph = g
+        for _ in range(todo):
+            st.graph.replay()
+        return torch.cat([ids, first.reshape(1, 1), st.tokens[:max_new_tokens - 1].reshape(1, -1)], 1)
+
+    def release_graphs(self) -> None:
+        """Drops the captured step (release before destroying the process group)."""
+        self._graph_state = None
+
+    def close(self) -> None:
+        self.release_graphs()
 
     def head_logits(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's vocab shard of the logits."""
@@ -433,6 +604,20 @@ class CompressedTPDecoder(TPDecoder):
         self.overlap = bool(overlap)
         self._dec_stream = torch.cuda.Stream(self.dev) if self.overlap else None
         self._ahead: dict = {}
+        # decoded weights land in preallocated output sets (two when the decode of layer
+        # i+1 overlaps layer i's projections), so descriptors are built once per
+        # (layer, image, set) and nothing is allocated per layer
+        self._views: list = []
+        per_layer = [self._out_layout(segs) for segs in self.segs]
+        set_elems = max([n for _, n in per_layer] + [1])
+        self._out_sets = [torch.empty(set_elems, dtype=torch.bfloat16, device=self.dev)
+                          for _ in range(2 if self.overlap else 1)]
+        self._out_offs = [o for o, _ in per_layer]
+        self._set_free = [None] * len(self._out_sets)
+        if self.head is not None:
+            g = self.head[0]
+            rows = min(self.head_block_rows, g.ss.rows)
+            self._head_buf = torch.empty(rows * g.ss.cols_decoded, dtype=torch.bfloat16, device=self.dev)
         if mode == "compressed":
             self.images = []
             for i in range(self.n_layers):
@@ -464,7 +649,10 @@ class CompressedTPDecoder(TPDecoder):
             cs.wait_event(self._consumed[slot])
         src = self.host[layer]
         with torch.cuda.stream(cs):
+            t0 = _mark(cs) if self.timeline is not None else None
             self.slots[slot][:src.numel()].copy_(src, non_blocking=True)
+            if t0 is not None:
+                self.timeline.append(("upload", layer, t0, _mark(cs)))
             ev = torch.cuda.Event()
             ev.record(cs)
         self.h2d_bytes += src.numel()
@@ -494,62 +682,90 @@ class CompressedTPDecoder(TPDecoder):
         self._issue_upload(nxt)
 
     # -- decode ----------------------------------------------------------------
-    def _descs(self, i: int, segs: list[_Seg], base: torch.Tensor, tag, outs: list[torch.Tensor]):
-        key = (i, tag, tuple(o.data_ptr() for o in outs))
-        d = self._desc_cache.get(key)
-        if d is None:
-            d = (_lib.StreamDesc * len(segs))()
-            for j, (g, o) in enumerate(zip(segs, outs)):
-                ss = g.ss
-                ds = _device.DeviceStream(packed=base[g.packed_off:g.packed_off + g.packed_cap], nbytes=g.packed_n,
-                                          capacity=g.packed_cap, offset_base=0,
-                                          offsets=base[g.offs_off:g.offs_off + 4 * max(g.n_chunks, 1)].view(torch.int32),
-                                          chunk_nbytes=base[g.nbs_off:g.nbs_off + 4 * max(g.n_chunks, 1)].view(torch.int32),
-                                          chunk_base=0)
-                e0 = ss.elem_lo
-                e1 = e0 + ss.rows * ss.cols_decoded
-                d[j] = _device.make_desc(ds, g.tables, ss.layer.encoded, e0, e1, o, base[g.sm_off + e0:])
-            if len(self._desc_cache) > 8 * self.n_layers + 16:
-                self._desc_cache.clear()
-            self._desc_cache[key] = d
-        return d
+    @staticmethod
+    def _out_layout(segs: list[_Seg]) -> tuple[list[int], int]:
+        offs, pos = [], 0
+        for g in segs:
+            offs.append(pos)
+            pos += (g.ss.rows * g.ss.cols_decoded + 127) // 128 * 128
+        return offs, pos
 
-    def _decode_layer(self, i: int, stream) -> dict:
-        """Enqueues layer i's decode on `stream`; returns name -> weight."""
-        p = "model.layers.%d." % i
+    @staticmethod
+    def _desc(g: _Seg, base: torch.Tensor, e0: int, out: torch.Tensor):
+        ds = _device.DeviceStream(packed=base[g.packed_off:g.packed_off + g.packed_cap], nbytes=g.packed_n,
+                                  capacity=g.packed_cap, offset_base=0,
+                                  offsets=base[g.offs_off:g.offs_off + 4 * max(g.n_chunks, 1)].view(torch.int32),
+                                  chunk_nbytes=base[g.nbs_off:g.nbs_off + 4 * max(g.n_chunks, 1)].view(torch.int32),
+                                  chunk_base=0)
+        return _device.make_desc(ds, g.tables, g.ss.layer.encoded, e0, e0 + out.numel(), out, base[g.sm_off + e0:])
+
+    def _layer_plan(self, i: int, slot: int, oset: int):
+        """(descriptor array, name -> weight view) for decoding layer i from
+        image `slot` (-1: its resident image) into output set `oset`."""
+        key = (i, slot, oset)
+        plan = self._desc_cache.get(key)
+        if plan is None:
+            segs = self.segs[i]
+            base = self.images[i] if slot < 0 else self.slots[slot]
+            buf = self._out_sets[oset]
+            p = "model.layers.%d." % i
+            d = (_lib.StreamDesc * max(1, len(segs)))()
+            views = {}
+            for j, (g, off) in enumerate(zip(segs, self._out_offs[i])):
+                ss = g.ss
+                o = buf[off:off + ss.rows * ss.cols_decoded]
+                d[j] = self._desc(g, base, ss.elem_lo, o)
+                views[g.key[len(p):]] = (o.view(ss.rows, ss.cols_decoded), ss)
+            plan = (d, views)
+            self._desc_cache[key] = plan
+        return plan
+
+    def _decode_layer(self, i: int, stream, oset: int) -> dict:
+        """Enqueues layer i's decode on `stream` into output set `oset`;
+        returns name -> weight (views of the set)."""
         segs = self.segs[i]
-        W = {}
         with torch.cuda.stream(stream):
             image, slot, ev = self._take_image(i)
             if ev is not None:
                 stream.wait_event(ev)
-            outs = [torch.empty(g.ss.rows, g.ss.cols_decoded, dtype=torch.bfloat16, device=self.dev) for g in segs]
+            if self._set_free[oset] is not None and self.overlap:
+                stream.wait_event(self._set_free[oset])
+            descs, views = self._layer_plan(i, slot, oset)
             if segs:
-                self.decoder.launch(self._descs(i, segs, image, slot, outs), len(segs))
+                t0 = _mark(stream) if self.timeline is not None else None
+                self.decoder.launch(descs, len(segs))
+                if t0 is not None:
+                    self.timeline.append(("decode", i, t0, _mark(stream)))
             self._release_image(slot, stream)
-            for g, o in zip(segs, outs):
-                ss = g.ss
-                W[g.key[len(p):]] = o if (ss.col_lo == 0 and ss.cols == ss.cols_decoded) else \
+            W = {}
+            for name, (o, ss) in views.items():
+                W[name] = o if (ss.col_lo == 0 and ss.cols == ss.cols_decoded) else \
                     o[:, ss.col_lo:ss.col_lo + ss.cols].contiguous()
         return W
+
+    def begin_forward(self) -> None:
+        if self.overlap:
+            # the side stream starts from everything enqueued so far (and joins a graph capture)
+            self._ahead.clear()
+            self._set_free = [None] * len(self._out_sets)
+            self._dec_stream.wait_stream(torch.cuda.current_stream(self.dev))
 
     def layer_weights(self, i: int) -> dict:
         compute = torch.cuda.current_stream(self.dev)
         if not self.overlap:
-            W = self._decode_layer(i, compute)
+            W = self._decode_layer(i, compute, 0)
         else:
             ds = self._dec_stream
+            # every op of layer i-1 is enqueued: its output set is free once they have run
+            self._set_free[(i - 1) % 2] = self._event(compute)
             if i not in self._ahead:
-                self._ahead[i] = (self._decode_layer(i, ds), self._event(ds))
+                self._ahead[i] = (self._decode_layer(i, ds, i % 2), self._event(ds))
             W, ev = self._ahead.pop(i)
             compute.wait_event(ev)
-            for t in W.values():
-                t.record_stream(compute)
             # the next layer decodes on the side stream while this one's projections run
-            # (fresh outputs from the caching allocator: nothing on the compute stream to wait for)
             nxt = i + 1
             if nxt < self.n_layers:
-                self._ahead[nxt] = (self._decode_layer(nxt, ds), self._event(ds))
+                self._ahead[nxt] = (self._decode_layer(nxt, ds, nxt % 2), self._event(ds))
         p = "model.layers.%d." % i
         # norms, and projections the store kept raw (incompressible), are resident as-is
         for key in self.layer_keys[i]:
@@ -571,24 +787,37 @@ class CompressedTPDecoder(TPDecoder):
         rows, cols = ss.rows, ss.cols
         out = torch.empty(x.shape[0], rows, dtype=x.dtype, device=self.dev)
         blk = self.head_block_rows
-        buf = torch.empty(min(blk, rows) * ss.cols_decoded, dtype=torch.bfloat16, device=self.dev)
         for r0 in range(0, rows, blk):
             r1 = min(rows, r0 + blk)
-            w = buf[:(r1 - r0) * ss.cols_decoded]
-            e0 = ss.elem_lo + r0 * ss.cols_decoded
-            ds = _device.DeviceStream(packed=image[g.packed_off:g.packed_off + g.packed_cap], nbytes=g.packed_n,
-                                      capacity=g.packed_cap, offset_base=0,
-                                      offsets=image[g.offs_off:g.offs_off + 4 * max(g.n_chunks, 1)].view(torch.int32),
-                                      chunk_nbytes=image[g.nbs_off:g.nbs_off + 4 * max(g.n_chunks, 1)].view(torch.int32),
-                                      chunk_base=0)
-            d = (_lib.StreamDesc * 1)()
-            d[0] = _device.make_desc(ds, g.tables, ss.layer.encoded, e0, e0 + w.numel(), w, image[g.sm_off + e0:])
+            key = ("head", r0)
+            plan = self._desc_cache.get(key)
+            if plan is None:
+                w = self._head_buf[:(r1 - r0) * ss.cols_decoded]
+                d = (_lib.StreamDesc * 1)()
+                d[0] = self._desc(g, image, ss.elem_lo + r0 * ss.cols_decoded, w)
+                plan = (d, w.view(r1 - r0, ss.cols_decoded)[:, ss.col_lo:ss.col_lo + cols])
+                self._desc_cache[key] = plan
+            d, wv = plan
             self.decoder.launch(d, 1)
-            wv = w.view(r1 - r0, ss.cols_decoded)[:, ss.col_lo:ss.col_lo + cols]
             out[:, r0:r1] = F.linear(x, wv)
         return out
 
+    def decode_bytes_per_forward(self) -> int:
+        """Algorithmic bytes one forward's decodes move on this rank:
+        sign/mantissa + packed stream + 4-byte chunk offsets + the 32 KiB
+        first-level table per tensor, plus 2 bytes per BF16 written."""
+        total = 0
+        segs = [g for layer in self.segs for g in layer] + ([self.head[0]] if self.head is not None else [])
+        for g in segs:
+            n = g.ss.rows * g.ss.cols_decoded
+            total += n + g.packed_n + 4 * g.n_chunks + 32768 + 2 * n
+        return total
+
+    def h2d_bytes_per_forward(self) -> int:
+        return sum(int(h.numel()) for h in self.host) if self.mode == "streamed" else 0
+
     def close(self) -> None:
+        super().close()
         if self.mode == "streamed":
             self.copy_stream.synchronize()
             torch.cuda.synchronize(self.dev)

@@ -284,6 +284,163 @@ def run_tokens(args, dev) -> dict:
         shutil.rmtree(root, ignore_errors=True)
 
 
+def _shared_tmpdir(world: int, rank: int, prefix: str) -> pathlib.Path:
+    root = None
+    if rank == 0:
+        root = tempfile.mkdtemp(prefix=prefix, dir="/dev/shm" if os.path.isdir("/dev/shm") else None)
+    if world > 1:
+        box = [root]
+        torch.distributed.broadcast_object_list(box, src=0)
+        root = box[0]
+    return pathlib.Path(root)
+
+
+def _max_over_ranks(v: float, world: int, dev) -> float:
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def allreduce_probe(world: int, dev, hidden: int, count: int) -> dict | None:
+    """The per-block exchange of tensor-parallel decoding: `count`
+    back-to-back all-reduces of one token's hidden state (BF16), timed with
+    CUDA events, max over ranks; bus bandwidth against the measured NVLink
+    peer-copy rate (latency-bound at this size)."""
+    if world < 2:
+        return None
+    x = torch.randn(1, hidden, device=dev).to(torch.bfloat16)
+    for _ in range(20):
+        torch.distributed.all_reduce(x)
+    torch.cuda.synchronize()
+    _barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(count):
+        torch.distributed.all_reduce(x)
+    b.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(a.elapsed_time(b), world, dev)
+    per_us = ms * 1e3 / count
+    nbytes = hidden * 2
+    bus = 2 * (world - 1) / world * nbytes / (per_us * 1e-6) / 1e9
+    return {"all_reduces_per_token": count, "bytes_each": nbytes, "us_each": round(per_us, 2),
+            "bus_gbps": round(bus, 3), "nvlink_peak_gbps": 770.0, "frac": round(bus / 770.0, 6),
+            "note": "one token's hidden state per all-reduce: latency-bound, far below link bandwidth"}
+
+
+def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
+    """Greedy tokens/s of the Qwen3-14B shape through
+    the tensor-parallel decoder on `world` GPUs (one rank per GPU; world=1
+    is a single GPU): every rank decodes only its own column/row shards of
+    every layer, one NCCL all-reduce after o_proj and after down_proj.
+      streamed:            compressed shards in page-locked host memory,
+                           copied to the GPU one layer at a time (the layer
+                           streamer over PCIe; device memory stays a few GB);
+      compressed_resident: compressed shards resident in HBM, decoded per
+                           layer per forward, the next layer's decode
+                           overlapping this layer's projections.
+    Timed: prompt (64 uniform ids) + new_tokens greedy tokens, CUDA events,
+    max over ranks. The store is written once (rank 0, TP-ready chunking)."""
+    from transformers import Qwen3Config
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, write_store
+    from afterimage_b200.runtime.tp_decoder import KVCache, load_tp_decoder, timeline_summary, _mark
+    import shutil
+    cfg = Qwen3Config(**QWEN3_14B)
+    root = _shared_tmpdir(world, rank, "aib_tp_")
+    store = root / "qwen3-14b-tp8"
+    out = {"model": "Qwen3-14B shape, random N(0,0.02)", "tp": world, "prompt_tokens": 64,
+           "new_tokens": args.new_tokens}
+    try:
+        if rank == 0:
+            t0 = time.perf_counter()
+            m = write_store(synthetic_checkpoint(cfg, 14, dev), store, EngineConfig(chunk_size=1024), tied=False,
+                            model_id="synthetic/qwen3-14b-shape", progress_every=0, tp_row_chunks=8)
+            out.update(store_gb=round(m["total_comp_bytes"] / 1e9, 2), ratio=round(m["ratio"], 4),
+                       store_build_s=round(time.perf_counter() - t0, 1),
+                       store_chunking="chunk_size 1024; o_proj 640, down_proj 1088 (whole chunks per rank up to TP 8)")
+        _barrier(world)
+        prompt = torch.randint(0, cfg.vocab_size, (1, 64), generator=torch.Generator().manual_seed(64))
+        seqs = {}
+        for name, resident, kw in (("streamed", "streamed", {}),
+                                   ("compressed_resident", "compressed", {"overlap": True})):
+            t0 = time.perf_counter()
+            dec = load_tp_decoder(store, cfg, world, rank, None, dev, resident=resident, **kw)
+            torch.cuda.synchronize()
+            load_s = _max_over_ranks(time.perf_counter() - t0, world, dev)
+            dec.generate_greedy(prompt, 1)  # warm: kernels, tables, allocator, NCCL
+            torch.cuda.synchronize()
+            torch.cuda.reset_peak_memory_stats(dev)
+            _barrier(world)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            seq = dec.generate_greedy(prompt, args.new_tokens)
+            b.record()
+            torch.cuda.synchronize()
+            ms = _max_over_ranks(a.elapsed_time(b), world, dev)
+            peak = _max_over_ranks(torch.cuda.max_memory_allocated(dev) / 1e9, world, dev)
+            seqs[name] = seq.cpu()
+            # one single-token forward with the event timeline (after the timed region)
+            cache = KVCache(dec.n_layers, dec.nkv, dec.hd, 80, dec.device)
+            dec.forward(prompt, cache)
+            torch.cuda.synchronize()
+            dec.timeline = []
+            base = _mark(torch.cuda.current_stream(dev))
+            dec.forward(seq[:, 64:65], cache)
+            torch.cuda.synchronize()
+            tl = timeline_summary(dec.timeline, base)
+            dec.timeline = None
+            events = tl.pop("events")
+            step_ms = _max_over_ranks(tl["span_ms"], world, dev)
+            dbytes = dec.decode_bytes_per_forward()
+            dec_ms = tl.get("decode_busy_ms", 0.0)
+            peak_hbm, _ = measured_peak()
+            info = {"tokens_per_s": round(args.new_tokens / (ms / 1e3), 3),
+                    "s_per_token": round(ms / 1e3 / args.new_tokens, 4), "load_s": round(load_s, 1),
+                    "peak_vram_gb_per_rank": round(peak, 2),
+                    "decode_step_ms": round(step_ms, 3), "timeline_rank0": tl,
+                    "decode_bytes_per_forward_per_rank": dbytes,
+                    "decode_gbps_in_step": round(dbytes / (dec_ms / 1e3) / 1e9, 1) if dec_ms else None,
+                    "decode_hbm_frac": round(dbytes / (dec_ms / 1e3) / 1e9 / peak_hbm, 4) if dec_ms else None}
+            if resident != "streamed":
+                # the single-token step captured once as a CUDA graph and replayed per token
+                dec.generate_greedy_graphed(prompt, args.new_tokens)  # warm + capture
+                torch.cuda.synchronize()
+                _barrier(world)
+                a.record()
+                gseq = dec.generate_greedy_graphed(prompt, args.new_tokens)
+                b.record()
+                torch.cuda.synchronize()
+                gms = _max_over_ranks(a.elapsed_time(b), world, dev)
+                info["graphed"] = {"tokens_per_s": round(args.new_tokens / (gms / 1e3), 3),
+                                   "s_per_token": round(gms / 1e3 / args.new_tokens, 4),
+                                   "tokens_equal_eager": bool(torch.equal(gseq.cpu(), seqs[name]))}
+                dec.release_graphs()
+            if resident == "streamed":
+                hb = dec.h2d_bytes_per_forward()
+                up = tl.get("upload_busy_ms", 0.0)
+                info.update(h2d_bytes_per_forward_per_rank=hb,
+                            h2d_gbps_in_step=round(hb / (up / 1e3) / 1e9, 1) if up else None)
+                dec.close()
+            if rank == 0 and name == "compressed_resident":
+                (root / "timeline_events.json").write_text(json.dumps(events))
+            out[name] = info
+            del dec, cache
+            torch.cuda.empty_cache()
+        out["tokens_equal_across_modes"] = bool(torch.equal(seqs["streamed"], seqs["compressed_resident"]))
+        out["all_reduce"] = allreduce_probe(world, dev, cfg.hidden_size, 2 * cfg.num_hidden_layers)
+        return out
+    finally:
+        _barrier(world)
+        if rank == 0:
+            shutil.rmtree(root, ignore_errors=True)
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -345,6 +502,8 @@ def main(argv=None) -> int:
     ap.add_argument("--tokens", action="store_true",
                     help="also measure greedy tokens/s on a Qwen3-14B-shaped model (builds a ~20 GB store)")
     ap.add_argument("--new-tokens", type=int, default=4)
+    ap.add_argument("--no-tp-tokens", action="store_true",
+                    help="skip the tensor-parallel tokens/s measurement (builds a ~20 GB store in /dev/shm)")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
 
@@ -448,12 +607,18 @@ def main(argv=None) -> int:
                "path": "LayerDecoder.decode_host on pinned host layers (upload, tables, one batched decode, status D2H)"}
 
     cpu = None
-    if rank == 0 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_baseline(host_layers[0])
-    tokens = None
-    if args.tokens and rank == 0:
-        del resident, descs, outs, host_layers
+    tokens = tp_tokens = None
+    if not args.no_tp_tokens or args.tokens:
+        del resident, descs, outs
         torch.cuda.empty_cache()
+    if not args.no_tp_tokens:
+        try:
+            tp_tokens = run_tp_tokens(args, world, rank, dev)
+        except Exception as exc:  # reported in the line; the decode measurement above stands
+            tp_tokens = {"error": "%s: %s" % (type(exc).__name__, exc)}
+    if args.tokens and rank == 0:
         tokens = run_tokens(args, dev)
 
     if rank == 0:
@@ -476,6 +641,8 @@ def main(argv=None) -> int:
             "e2e": e2e,
             "cpu_baseline": cpu,
         }
+        if tp_tokens is not None:
+            line["tokens_qwen3_14b_tp"] = tp_tokens
         if tokens is not None:
             line["tokens_per_s_qwen3_14b"] = tokens
         print(json.dumps(line), flush=True)

@@ -73,6 +73,40 @@ def test_layer_image_layout_round_trips():
         assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("inf,parts,want", [(5120, 8, 640), (17408, 8, 1088), (17408, 1, 1024), (17408, 2, 1088),
+                                           (14336, 8, 896), (4096, 8, 512), (32768, 8, 1024), (3072, 8, 384),
+                                           (5120, 3, 1024), (896, 4, 224), (320, 4, 80), (1031 * 8, 8, 1024),
+                                           (5120, 4, 1280), (5120, 2, 1280), (1000 * 8, 8, 1000)])
+def test_tp_chunk_size(inf, parts, want):
+    from afterimage_b200.runtime.streaming_engine import tp_chunk_size
+    cs = tp_chunk_size(inf, parts, 1024)
+    assert cs == want
+    if cs != 1024:
+        assert (inf // parts) % cs == 0
+
+
+class _Ev:
+    def __init__(self, t):
+        self.t = t
+
+    def elapsed_time(self, other):
+        return other.t - self.t
+
+
+def test_timeline_summary_interval_math():
+    from afterimage_b200.runtime.tp_decoder import timeline_summary
+    base = _Ev(0.0)
+    tl = [("decode", 0, _Ev(0.0), _Ev(1.0)), ("compute", 0, _Ev(1.0), _Ev(3.0)),
+          ("decode", 1, _Ev(1.5), _Ev(2.5)), ("compute", 1, _Ev(3.0), _Ev(4.0)),
+          ("upload", 2, _Ev(0.5), _Ev(5.0))]
+    out = timeline_summary(tl, base)
+    assert out["span_ms"] == 5.0
+    assert out["decode_busy_ms"] == 2.0 and out["compute_busy_ms"] == 3.0
+    assert out["decode_overlapped_ms"] == 1.0       # [1.5, 2.5] inside compute [1, 4]
+    assert out["upload_overlapped_ms"] == 3.5       # upload [0.5, 5] against busy [0, 4]
+    assert len(out["events"]) == 5
+
+
 def test_shard_kinds():
     assert shard_kind("model.layers.3.self_attn.q_proj.weight") == "col"
     assert shard_kind("model.layers.3.mlp.down_proj.weight") == "row"

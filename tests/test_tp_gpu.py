@@ -71,6 +71,30 @@ def test_tp_single_gpu_matches_transformers(stores, resident, kw, which):
         dec.close()
 
 
+@pytest.mark.parametrize("resident,kw", [("decoded", {}), ("compressed", {}), ("compressed", {"overlap": True})])
+def test_tp_graphed_generation(stores, resident, kw):
+    """The single-token step captured as a CUDA graph (decode launches
+    included) gives the greedy tokens of the eager decoder and of
+    transformers; a second call replays the same graph."""
+    from afterimage_b200.runtime.tp_decoder import load_tp_decoder
+    cfg, model, store, tp_store = stores
+    dec = load_tp_decoder(tp_store, cfg, 1, 0, None, "cuda", resident=resident, **kw)
+    model = model.to("cuda")
+    for seed in (3, 4):
+        ids = torch.randint(0, cfg.vocab_size, (1, 9), device="cuda",
+                            generator=torch.Generator(device="cuda").manual_seed(seed))
+        seq = dec.generate_greedy_graphed(ids, 6)
+        eager = dec.generate_greedy(ids, 6)
+        ref_seq, margins = _ref_greedy(model, ids, 6)
+        _check_greedy(seq, ref_seq, margins, 9)
+        _check_greedy(seq, eager, margins, 9)
+        assert seq.shape == (1, 15)
+    assert dec._graph_state is not None and dec._graph_state.graph is not None
+    if resident != "decoded":
+        _lib_status_clear()
+    dec.close()
+
+
 def _lib_status_clear():
     from afterimage_b200.runtime import _device
     _device.check_status(torch.device("cuda", torch.cuda.current_device()))
@@ -108,7 +132,10 @@ def _rank_main(rank, world, port, tp_store, cfg_dict, ids, q, resident):
         dec = load_tp_decoder(tp_store, cfg, world, rank, None, "cuda:%d" % rank, resident=resident)
         logits = dec.forward(ids.to("cuda:%d" % rank)).float().cpu().numpy()
         seq = dec.generate_greedy(ids.to("cuda:%d" % rank), 5).cpu().numpy()
-        q.put((rank, logits, seq))
+        gseq = dec.generate_greedy_graphed(ids.to("cuda:%d" % rank), 5).cpu().numpy() \
+            if resident != "streamed" else seq
+        dec.release_graphs()
+        q.put((rank, logits, seq, gseq))
         if resident == "streamed":
             dec.close()
     finally:
@@ -135,8 +162,10 @@ def test_tp_two_gpus_nccl_matches_transformers(stores, resident):
     model = model.to("cuda:0")
     with torch.no_grad():
         ref = model(input_ids=ids.to("cuda:0")).logits[0].float().cpu()
-    for rank, logits, seq in got:
+    for rank, logits, seq, gseq in got:
         logits = torch.from_numpy(logits)
         assert torch.allclose(logits, ref, atol=3e-2, rtol=0), float((logits - ref).abs().max())
     ref_seq, margins = _ref_greedy(model, ids.to("cuda:0"), 5)
     _check_greedy(torch.from_numpy(got[0][2]), ref_seq.cpu(), margins, 11)
+    _check_greedy(torch.from_numpy(got[0][3]), ref_seq.cpu(), margins, 11)
+    assert (got[0][3] == got[1][3]).all()  # ranks agree
