@@ -576,7 +576,7 @@ class CompressedTPDecoder(TPDecoder):
     decoded on a side stream while layer i's projections run."""
 
     def __init__(self, hf_cfg, weights: dict, streams: dict, world=1, rank=0, group=None, device="cuda",
-                 mode: str = "compressed", slots: int = 2, head_block_rows: int = 16384, overlap: bool = False):
+                 mode: str = "compressed", slots: int = 3, head_block_rows: int = 16384, overlap: bool = False):
         super().__init__(hf_cfg, weights, world, rank, group, device)
         if mode not in ("compressed", "streamed"):
             raise ValueError("mode must be 'compressed' or 'streamed'")
