@@ -56,6 +56,17 @@ class StreamDesc(ctypes.Structure):
     ]
 
 
+class GemvDesc(ctypes.Structure):
+    """aib_gemv_desc (include/afterimage_b200.h)."""
+    _fields_ = [
+        ("stream", StreamDesc),
+        ("cols", I64),
+        ("x", P),
+        ("partial", P),
+        ("y", P),
+    ]
+
+
 # (name, restype, argtypes) of every exported entry point; tests check that
 # the header declares exactly these.
 SIGNATURES = [
@@ -75,6 +86,7 @@ SIGNATURES = [
     ("aib_decode_exponents_u8", CI, [ctypes.POINTER(StreamDesc), P, P]),
     ("aib_decode_exponents_i32", CI, [ctypes.POINTER(StreamDesc), P, P]),
     ("aib_decode_bf16_batch", CI, [ctypes.POINTER(StreamDesc), CI, P, P]),
+    ("aib_decode_gemv_bf16_batch", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
     ("aib_recombine", CI, [P, P, I64, P, P]),
 ]
 

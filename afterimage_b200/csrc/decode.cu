@@ -25,6 +25,7 @@
 //     writes 16-byte vectorised BF16 stores, 128 contiguous bytes per chunk.
 // The decoder uses no tensor cores and no scratch global memory: the
 // exponent never round-trips through HBM.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -79,6 +80,12 @@ namespace aib {
 #endif
 #ifndef AIB_AHEAD
 #define AIB_AHEAD 1
+#endif
+// Launches with fewer groups than a wave of warps spread them over every SM
+// (fewer active warps per CTA) instead of filling few CTAs; groups are
+// dealt to CTAs round-robin.
+#ifndef AIB_SPREAD
+#define AIB_SPREAD 1
 #endif
 constexpr int kFastBits = AIB_FAST_BITS;
 constexpr int kFastSize = 1 << kFastBits;
@@ -383,49 +390,18 @@ __device__ __forceinline__ void emit(uint2 e, uint32_t &olo, uint32_t &ohi, int 
   }
 }
 
-// CSC != 0 specialises the kernel for one chunk size (the reference's
-// default, 1024), making the merge's address offsets compile-time constants.
+// A warp's first group of its job; later ones follow every ctas * kWarps.
+__device__ __forceinline__ int64_t first_group(int cta_begin, int ctas, int warp) {
+  const int64_t b = static_cast<int64_t>(blockIdx.x) - cta_begin;
+  return AIB_SPREAD ? b + static_cast<int64_t>(warp) * ctas : b * kWarps + warp;
+}
+
+// The group loop: every warp decodes groups of 32 consecutive chunks of job
+// J. CSC != 0 makes the chunk size a compile-time constant (the merge's
+// address offsets become immediates).
 template <int MODE, int CSC>
-__global__ void __launch_bounds__(kThreads, AIB_MIN_BLOCKS) decode_kernel(const __grid_constant__ Batch batch,
-                                                                          int32_t *status) {
-  extern __shared__ __align__(128) unsigned char smem[];
-  __shared__ uint64_t bar;
-
-  int jsel = 0;
-  for (int t = 1; t < batch.count; ++t)
-    if (static_cast<int>(blockIdx.x) >= batch.job[t].cta_begin) jsel = t;
-  const Job &J = batch.job[jsel];
-
-  uint2 *s_fast = reinterpret_cast<uint2 *>(smem);
-  if (threadIdx.x == 0) {
-    mbar_init(&bar, 1);
-    mbar_expect_tx(&bar, kFastBytes);
-    bulk_g2s(s_fast, J.fast, kFastBytes, &bar);
-  }
-  __syncthreads();
-  {
-    unsigned spins = 0;
-    int timed_out = 0;
-    while (!mbar_try_wait(&bar, 0)) {
-      if (++spins > kWaitLimit) {
-        timed_out = 1;
-        break;
-      }
-      __nanosleep(64);
-    }
-    // the whole CTA leaves together so no barrier below misses a thread
-    if (__syncthreads_or(timed_out)) {
-      if (status && threadIdx.x == 0) atomicOr(status, AIB_STATUS_WAIT_TIMEOUT);
-      return;
-    }
-  }
-  if (*J.flags != 0) {
-    // not a prefix-code LUT (or out-of-range entries): route every lookup
-    // through the reference LUT itself
-    for (int i = threadIdx.x; i < kFastSize; i += kThreads) s_fast[i] = make_uint2(0u, 0u);
-    __syncthreads();
-  }
-
+__device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast, unsigned char *smem,
+                                              int32_t *status) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   unsigned char *ring_base = smem + kFastBytes + warp * kRingWarpBytes;
@@ -446,7 +422,7 @@ __global__ void __launch_bounds__(kThreads, AIB_MIN_BLOCKS) decode_kernel(const 
   const uint64_t pol_keep = policy_keep();
   const uint64_t pol_once = policy_stream();
 
-  for (int64_t grp = static_cast<int64_t>(blockIdx.x - J.cta_begin) * kWarps + warp; grp < J.n_groups;
+  for (int64_t grp = first_group(J.cta_begin, J.ctas, warp); grp < J.n_groups;
        grp += static_cast<int64_t>(J.ctas) * kWarps) {
     const int64_t c0 = J.c_begin + grp * 32;
     const int64_t c = c0 + lane;
@@ -601,6 +577,277 @@ __global__ void __launch_bounds__(kThreads, AIB_MIN_BLOCKS) decode_kernel(const 
   }
 }
 
+// Stages a tensor's first-level table into shared memory with one bulk copy
+// (TMA 1-D, mbarrier completion, bounded wait) and zeroes it when the
+// table's flags say the reference LUT is not a plain prefix-code table
+// (every lookup then takes the exact slow path). Returns false, uniformly
+// for the CTA, when the copy did not complete in time.
+__device__ __forceinline__ bool stage_table(uint2 *s_fast, const uint2 *src, const int32_t *flags, uint64_t *bar,
+                                            int32_t *status) {
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    mbar_expect_tx(bar, kFastBytes);
+    bulk_g2s(s_fast, src, kFastBytes, bar);
+  }
+  __syncthreads();
+  unsigned spins = 0;
+  int timed_out = 0;
+  while (!mbar_try_wait(bar, 0)) {
+    if (++spins > kWaitLimit) {
+      timed_out = 1;
+      break;
+    }
+    __nanosleep(64);
+  }
+  // the whole CTA leaves together so no barrier below misses a thread
+  if (__syncthreads_or(timed_out)) {
+    if (status && threadIdx.x == 0) atomicOr(status, AIB_STATUS_WAIT_TIMEOUT);
+    return false;
+  }
+  if (*flags != 0) {
+    for (int i = threadIdx.x; i < kFastSize; i += blockDim.x) s_fast[i] = make_uint2(0u, 0u);
+    __syncthreads();
+  }
+  return true;
+}
+
+// CSC selects the group loop: 1024 (every job has the reference's default
+// chunk size), 0 (any chunk size) or -1 (per job: jobs with chunk size 1024
+// take the specialised loop, the others the general one; a CTA serves one
+// job, so the choice is uniform per CTA).
+template <int MODE, int CSC>
+__global__ void __launch_bounds__(kThreads, AIB_MIN_BLOCKS) decode_kernel(const __grid_constant__ Batch batch,
+                                                                          int32_t *status) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t bar;
+
+  int jsel = 0;
+  for (int t = 1; t < batch.count; ++t)
+    if (static_cast<int>(blockIdx.x) >= batch.job[t].cta_begin) jsel = t;
+  const Job &J = batch.job[jsel];
+
+  uint2 *s_fast = reinterpret_cast<uint2 *>(smem);
+  if (!stage_table(s_fast, J.fast, J.flags, &bar, status)) return;
+
+  if (CSC < 0) {
+    if (J.chunk_size == kDefaultChunk)
+      decode_groups<MODE, kDefaultChunk>(J, s_fast, smem, status);
+    else
+      decode_groups<MODE, 0>(J, s_fast, smem, status);
+  } else {
+    decode_groups<MODE, (CSC > 0 ? CSC : 0)>(J, s_fast, smem, status);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// fused decode -> GEMV: y = W x for one input vector (a single-token
+// projection), W read only in compressed form and never written out
+// ---------------------------------------------------------------------------
+// The range is whole rows of a row-major [rows, cols] tensor whose rows are
+// whole chunks (cols % chunk_size == 0). A warp takes 32 consecutive rows at
+// one column chunk j: lane l decodes chunk (row0 + l, j) on its own -- no
+// ring, no merge, no warp synchronisation inside the chunk -- and every
+// lane reads the same stretch x[j*cs ...] of the input (one broadcast
+// load). Each complete word of four exponents is combined with its four
+// sign/mantissa bytes into BF16 weights (the reference's _recombine,
+// compressed_store.py:94-114) and multiplied into an fp32 partial sum. The
+// chunk's partial is stored; a second kernel sums each row's partials in
+// column order and rounds to BF16, so the result is deterministic.
+struct GemvJob {
+  const uint8_t *packed;
+  int64_t packed_cap;
+  int64_t packed_nbytes;
+  int64_t offset_base;
+  const int32_t *offs;
+  const int32_t *nbytes;
+  int64_t chunk_base;
+  const uint2 *fast;
+  const int32_t *flags;
+  const int32_t *sym_lut;
+  const int8_t *len_lut;
+  const uint8_t *sm;     // element e0 at index 0
+  const uint16_t *x;     // bf16[cols]
+  float *partial;        // chunk (r, j) of the range at r * cpr + j
+  uint16_t *y;           // bf16[rows]
+  int64_t c0;            // global index of the range's first chunk
+  int64_t rows;
+  int64_t n_groups;      // ceil(rows / 32) * cpr
+  int64_t row_begin;     // rows of the batch's earlier jobs
+  int32_t cpr;           // chunks per row
+  int32_t chunk_size;
+  int32_t max_bits;
+  int32_t cta_begin;
+  int32_t ctas;
+  int32_t pad;
+};
+
+struct GemvBatch {
+  GemvJob job[AIB_MAX_BATCH];
+  int32_t count;
+};
+
+constexpr int kGemvSmemBytes = kFastBytes + kThreads * kSlotRow;
+
+// Sign/mantissa bytes of a lane's chunk, read 16 at a time two blocks ahead
+// of use (register queue: `cur` holds symbols [kb, kb + 16), `nxt` the 16
+// after), so the word multiply never waits on a global load.
+struct SmQueue {
+  uint4 cur, nxt;
+  int kb;
+};
+
+__device__ __forceinline__ uint4 ldg16(const uint8_t *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
+
+__device__ __forceinline__ void smq_init(SmQueue &q, const uint8_t *smp, int need) {
+  q.cur = need > 0 ? ldg16(smp) : make_uint4(0, 0, 0, 0);
+  q.nxt = need > 16 ? ldg16(smp + 16) : make_uint4(0, 0, 0, 0);
+  q.kb = 0;
+}
+
+// four weights (exponent bytes of `ew`, sign/mantissa word `sw`) times
+// x[k..k+3], accumulated in fp32
+__device__ __forceinline__ void dot4(uint32_t ew, uint32_t sw, int k, const uint16_t *xp, float &a0, float &a1) {
+  const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(xp + k));
+  const uint32_t M = 0x807F807Fu;
+  const uint32_t p01 = __byte_perm(ew, 0, 0x4140) * 128u + (__byte_perm(sw, 0, 0x1100) & M);
+  const uint32_t p23 = __byte_perm(ew, 0, 0x4342) * 128u + (__byte_perm(sw, 0, 0x3322) & M);
+  a0 = fmaf(__uint_as_float(p01 << 16), __uint_as_float(xv.x << 16), a0);
+  a1 = fmaf(__uint_as_float(p01 & 0xFFFF0000u), __uint_as_float(xv.x & 0xFFFF0000u), a1);
+  a0 = fmaf(__uint_as_float(p23 << 16), __uint_as_float(xv.y << 16), a0);
+  a1 = fmaf(__uint_as_float(p23 & 0xFFFF0000u), __uint_as_float(xv.y & 0xFFFF0000u), a1);
+}
+
+// emit() for the GEMV: a full word of four symbols is multiplied in at once
+// (only words inside the chunk: need is a multiple of four)
+__device__ __forceinline__ void emit_dot(uint2 e, uint32_t &olo, uint32_t &ohi, int &n8, int &k, int need,
+                                         SmQueue &q, const uint8_t *smp, const uint16_t *xp, float &a0,
+                                         float &a1) {
+  olo |= e.x << n8;
+  ohi |= __funnelshift_l(e.x, 0u, static_cast<uint32_t>(n8));
+  n8 += static_cast<int>(e.y >> 8);
+  if (n8 >= 32) {
+    if (k < need) {
+      const int w = (k >> 2) & 3;
+      const uint32_t sw = w == 0 ? q.cur.x : (w == 1 ? q.cur.y : (w == 2 ? q.cur.z : q.cur.w));
+      dot4(olo, sw, k, xp, a0, a1);
+      if (w == 3) {
+        q.cur = q.nxt;
+        q.kb += 16;
+        if (q.kb + 16 < need) q.nxt = ldg16(smp + q.kb + 16);
+      }
+    }
+    olo = ohi;
+    ohi = 0;
+    n8 -= 32;
+    k += 4;
+  }
+}
+
+template <int CSC>
+__device__ __forceinline__ void gemv_groups(const GemvJob &G, const uint2 *s_fast, unsigned char *smem,
+                                            int32_t *status) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  unsigned char *my_stream = smem + kFastBytes + (warp * 32 + lane) * kSlotRow;
+  const int cs = CSC ? CSC : G.chunk_size;
+  const int max_bits = G.max_bits;
+  const uint4 *src = reinterpret_cast<const uint4 *>(G.packed);
+  const int64_t bmax = G.packed_cap / 16 - 1;
+  const uint64_t pol_keep = policy_keep();
+  for (int64_t grp = first_group(G.cta_begin, G.ctas, warp); grp < G.n_groups;
+       grp += static_cast<int64_t>(G.ctas) * kWarps) {
+    const int64_t rb = grp / G.cpr;
+    const int j = static_cast<int>(grp - rb * G.cpr);
+    const int64_t row = rb * 32 + lane;
+    const bool active = row < G.rows;
+    const int64_t cl = row * G.cpr + j;  // chunk index within the range
+    const uint8_t *smp = G.sm + cl * cs;
+    const uint16_t *xp = G.x + static_cast<int64_t>(j) * cs;
+    Reader rd;
+    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.q0 = rd.q1 = rd.q2 = rd.q3 = 0; rd.qn = 4; rd.bi = 0;
+    rd.slot = 0;
+    if (active) {
+      const int64_t c = G.c0 + cl;
+      int64_t pos = static_cast<int64_t>(G.offs[c - G.chunk_base]) - G.offset_base;
+      const int64_t nbyt = G.nbytes[c - G.chunk_base];
+      if (pos < 0 || nbyt < 0 || pos + nbyt > G.packed_nbytes) {
+        if (status) atomicOr(status, AIB_STATUS_BAD_CHUNK_RANGE);
+        pos = 0;
+      }
+      reader_init(rd, my_stream, src, bmax, pos, pol_keep);
+      for (int q = 0; q < cs; q += 128) prefetch_l2(smp + q);
+    }
+    const int need = active ? cs : 0;
+    int k = 0, n8 = 0;
+    uint32_t olo = 0, ohi = 0;
+    float a0 = 0.f, a1 = 0.f;
+    SmQueue q;
+    smq_init(q, smp, need);
+    while (__any_sync(0xffffffffu, k < need)) {
+      if (k < need) {
+        if (rd.nb < 32) reader_refill(rd, my_stream, src, bmax, pol_keep);
+        uint32_t ymin = 0xFFFFFFFFu;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const uint2 e = s_fast[rd.ah >> (32 - kFastBits)];
+          ymin = min(ymin, e.y);
+          reader_consume(rd, e.y & 31u);
+          emit_dot(e, olo, ohi, n8, k, need, q, smp, xp, a0, a1);
+        }
+        if (__any_sync(__activemask(), ymin == 0u)) {
+          if (ymin == 0u) {
+            // a code longer than the table: the reference LUT (>= 20 valid bits here)
+            const uint32_t w = (rd.ah >> 16) >> (16 - max_bits);
+            const uint32_t sy = static_cast<uint32_t>(__ldg(G.sym_lut + w)) & 0xFFu;
+            const uint32_t l = static_cast<uint32_t>(static_cast<int>(__ldg(G.len_lut + w))) & 31u;
+            reader_consume(rd, l);
+            emit_dot(make_uint2(sy, 8u << 8), olo, ohi, n8, k, need, q, smp, xp, a0, a1);
+          }
+        }
+      }
+    }
+    if (active) G.partial[cl] = a0 + a1;
+    cp_async_wait<0>();
+  }
+}
+
+template <int CSC>
+__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvBatch batch,
+                                                           int32_t *status) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ uint64_t bar;
+  int jsel = 0;
+  for (int t = 1; t < batch.count; ++t)
+    if (static_cast<int>(blockIdx.x) >= batch.job[t].cta_begin) jsel = t;
+  const GemvJob &G = batch.job[jsel];
+  uint2 *s_fast = reinterpret_cast<uint2 *>(smem);
+  if (!stage_table(s_fast, G.fast, G.flags, &bar, status)) return;
+  if (CSC < 0) {
+    if (G.chunk_size == kDefaultChunk)
+      gemv_groups<kDefaultChunk>(G, s_fast, smem, status);
+    else
+      gemv_groups<0>(G, s_fast, smem, status);
+  } else {
+    gemv_groups<(CSC > 0 ? CSC : 0)>(G, s_fast, smem, status);
+  }
+}
+
+// y[r] = bf16(sum over j of partial[r * cpr + j]), j ascending
+__global__ void gemv_rows_kernel(const __grid_constant__ GemvBatch batch, int64_t total_rows) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  for (int64_t t = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; t < total_rows; t += stride) {
+    int jsel = 0;
+    for (int q = 1; q < batch.count; ++q)
+      if (t >= batch.job[q].row_begin) jsel = q;
+    const GemvJob &G = batch.job[jsel];
+    const int64_t r = t - G.row_begin;
+    const float *p = G.partial + r * G.cpr;
+    float acc = 0.f;
+    for (int q = 0; q < G.cpr; ++q) acc += p[q];
+    G.y[r] = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
+  }
+}
+
 __global__ void recombine_kernel(const uint8_t *__restrict__ e, const uint8_t *__restrict__ sm, int64_t n,
                                  uint16_t *__restrict__ out, int vec) {
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -624,6 +871,7 @@ __global__ void recombine_kernel(const uint8_t *__restrict__ e, const uint8_t *_
 struct DeviceInfo {
   int sms = 0;
   int occ[3] = {0, 0, 0};
+  int gemv_occ = 1;
   bool ready = false;
 };
 static DeviceInfo g_dev[64];
@@ -643,6 +891,7 @@ static int setup_kernel(int dev, DeviceInfo &di) {
   (void)dev;
   int rc = setup_one<MODE, 0>(di);
   if (rc == AIB_OK) rc = setup_one<MODE, kDefaultChunk>(di);
+  if (rc == AIB_OK) rc = setup_one<MODE, -1>(di);
   return rc;
 }
 
@@ -661,6 +910,13 @@ static int device_info(DeviceInfo **out) {
     if ((rc = setup_kernel<kModeBF16>(dev, di)) != AIB_OK) return rc;
     if ((rc = setup_kernel<kModeU8>(dev, di)) != AIB_OK) return rc;
     if ((rc = setup_kernel<kModeI32>(dev, di)) != AIB_OK) return rc;
+    AIB_CUDA(cudaFuncSetAttribute(gemv_kernel<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemBytes));
+    AIB_CUDA(cudaFuncSetAttribute(gemv_kernel<kDefaultChunk>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  kGemvSmemBytes));
+    AIB_CUDA(cudaFuncSetAttribute(gemv_kernel<-1>, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemvSmemBytes));
+    int occ = 0;
+    AIB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_kernel<-1>, kThreads, kGemvSmemBytes));
+    di.gemv_occ = std::max(1, occ);
     di.ready = true;
   }
   *out = &di;
@@ -771,24 +1027,124 @@ static int launch(const aib_stream_desc *descs, int count, int32_t *status, void
   // CTAs: as many as the work needs at kGroupsPerWarp groups per warp, capped
   // at a few full waves; split across jobs in proportion to their groups.
   const int64_t wave = static_cast<int64_t>(di->sms) * di->occ[MODE];
-  const int64_t want = (total_groups + kWarps * kGroupsPerWarp - 1) / (kWarps * kGroupsPerWarp);
+  int64_t want = (total_groups + kWarps * kGroupsPerWarp - 1) / (kWarps * kGroupsPerWarp);
+  if (AIB_SPREAD) want = std::max(want, std::min(total_groups, wave));
   const int64_t cap = std::max<int64_t>(want, 1) < 4 * wave ? std::max<int64_t>(want, 1) : 4 * wave;
   int cta = 0;
   for (int i = 0; i < n; ++i) {
     Job &j = batch.job[i];
     int64_t share = (cap * j.n_groups + total_groups - 1) / total_groups;
-    const int64_t max_useful = (j.n_groups + kWarps - 1) / kWarps;
+    const int64_t max_useful = AIB_SPREAD ? j.n_groups : (j.n_groups + kWarps - 1) / kWarps;
     share = std::max<int64_t>(1, std::min(share, max_useful));
     j.cta_begin = cta;
     j.ctas = static_cast<int32_t>(share);
     cta += j.ctas;
   }
-  bool all_default = true;
-  for (int i = 0; i < n; ++i) all_default = all_default && batch.job[i].chunk_size == kDefaultChunk;
-  if (all_default)
-    decode_kernel<MODE, kDefaultChunk><<<cta, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(batch, status);
+  int n_default = 0;
+  for (int i = 0; i < n; ++i) n_default += batch.job[i].chunk_size == kDefaultChunk;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_default == n)
+    decode_kernel<MODE, kDefaultChunk><<<cta, kThreads, kSmemBytes, st>>>(batch, status);
+  else if (n_default > 0)
+    decode_kernel<MODE, -1><<<cta, kThreads, kSmemBytes, st>>>(batch, status);
   else
-    decode_kernel<MODE, 0><<<cta, kThreads, kSmemBytes, static_cast<cudaStream_t>(stream)>>>(batch, status);
+    decode_kernel<MODE, 0><<<cta, kThreads, kSmemBytes, st>>>(batch, status);
+  AIB_CUDA(cudaGetLastError());
+  return AIB_OK;
+}
+
+static int gemv_launch(const aib_gemv_desc *descs, int count, int32_t *status, void *stream) {
+  if (count < 1 || count > AIB_MAX_BATCH) {
+    aib_set_errorf("batch count must be in [1, %d], got %d", AIB_MAX_BATCH, count);
+    return AIB_EINVAL;
+  }
+  if (!descs) return aib_set_error("null descriptor array"), AIB_EINVAL;
+  GemvBatch batch;
+  std::memset(&batch, 0, sizeof(batch));
+  int64_t total_groups = 0, total_rows = 0;
+  int n = 0;
+  for (int i = 0; i < count; ++i) {
+    const aib_gemv_desc *g = &descs[i];
+    const aib_stream_desc &d = g->stream;
+    if (d.elem_begin == d.elem_end && d.elem_begin >= 0 && d.elem_end <= d.n_symbols) continue;  // no rows
+    if (!g->x || !g->partial || !g->y) return aib_set_error("gemv: null x, partial or y"), AIB_EINVAL;
+    if (!aligned(g->x, 8) || !aligned(g->partial, 4) || !aligned(g->y, 2))
+      return aib_set_error("gemv: x must be 8-byte, partial 4-byte and y 2-byte aligned"), AIB_EINVAL;
+    if (d.chunk_size < 16 || d.chunk_size % 16)
+      return aib_set_errorf("gemv: chunk_size must be a positive multiple of 16, got %d", d.chunk_size), AIB_EINVAL;
+    if (g->cols < 1 || g->cols % d.chunk_size)
+      return aib_set_errorf("gemv: cols %lld must be a positive multiple of chunk_size %d", (long long)g->cols,
+                            d.chunk_size),
+             AIB_EINVAL;
+    if (d.elem_begin % g->cols || d.elem_end % g->cols)
+      return aib_set_error("gemv: the element range must be whole rows"), AIB_EINVAL;
+    if (!d.sign_mantissa || !aligned(d.sign_mantissa, 16))
+      return aib_set_error("gemv: sign_mantissa must be a 16-byte aligned device pointer"), AIB_EINVAL;
+    // the stream checks shared with the decode (out is not written here)
+    aib_stream_desc copy = d;
+    copy.out = g->y;
+    Job j;
+    bool empty = false;
+    const int rc = make_job(&copy, kModeBF16, &j, &empty);
+    if (rc != AIB_OK) return rc;
+    if (empty) continue;
+    GemvJob &G = batch.job[n];
+    G.packed = j.packed;
+    G.packed_cap = j.packed_cap;
+    G.packed_nbytes = j.packed_nbytes;
+    G.offset_base = j.offset_base;
+    G.offs = j.offs;
+    G.nbytes = j.nbytes;
+    G.chunk_base = j.chunk_base;
+    G.fast = j.fast;
+    G.flags = j.flags;
+    G.sym_lut = j.sym_lut;
+    G.len_lut = j.len_lut;
+    G.sm = j.sm;
+    G.x = static_cast<const uint16_t *>(g->x);
+    G.partial = g->partial;
+    G.y = static_cast<uint16_t *>(g->y);
+    G.c0 = d.elem_begin / d.chunk_size;
+    G.rows = (d.elem_end - d.elem_begin) / g->cols;
+    G.cpr = static_cast<int32_t>(g->cols / d.chunk_size);
+    G.n_groups = (G.rows + 31) / 32 * G.cpr;
+    G.row_begin = total_rows;
+    G.chunk_size = d.chunk_size;
+    G.max_bits = d.max_bits;
+    total_groups += G.n_groups;
+    total_rows += G.rows;
+    ++n;
+  }
+  if (n == 0) return AIB_OK;
+  DeviceInfo *di = nullptr;
+  int rc = device_info(&di);
+  if (rc != AIB_OK) return rc;
+  batch.count = n;
+  const int64_t wave = static_cast<int64_t>(di->sms) * di->gemv_occ;
+  int64_t want = std::max<int64_t>(1, (total_groups + kWarps - 1) / kWarps);
+  if (AIB_SPREAD) want = std::max(want, std::min(total_groups, wave));
+  const int64_t cap = std::min<int64_t>(want, 4 * wave);
+  int cta = 0;
+  int n_default = 0;
+  for (int i = 0; i < n; ++i) {
+    GemvJob &G = batch.job[i];
+    int64_t share = (cap * G.n_groups + total_groups - 1) / total_groups;
+    share = std::max<int64_t>(1, std::min(share, AIB_SPREAD ? G.n_groups : (G.n_groups + kWarps - 1) / kWarps));
+    G.cta_begin = cta;
+    G.ctas = static_cast<int32_t>(share);
+    cta += G.ctas;
+    n_default += G.chunk_size == kDefaultChunk;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (n_default == n)
+    gemv_kernel<kDefaultChunk><<<cta, kThreads, kGemvSmemBytes, st>>>(batch, status);
+  else if (n_default > 0)
+    gemv_kernel<-1><<<cta, kThreads, kGemvSmemBytes, st>>>(batch, status);
+  else
+    gemv_kernel<0><<<cta, kThreads, kGemvSmemBytes, st>>>(batch, status);
+  AIB_CUDA(cudaGetLastError());
+  const int64_t blocks = std::min<int64_t>((total_rows + 255) / 256, 4 * static_cast<int64_t>(di->sms));
+  gemv_rows_kernel<<<static_cast<int>(blocks), 256, 0, st>>>(batch, total_rows);
   AIB_CUDA(cudaGetLastError());
   return AIB_OK;
 }
@@ -846,6 +1202,10 @@ AIB_API int aib_decode_exponents_i32(const aib_stream_desc *desc, int32_t *d_sta
 
 AIB_API int aib_decode_bf16_batch(const aib_stream_desc *descs, int count, int32_t *d_status, void *stream) {
   return launch<kModeBF16>(descs, count, d_status, stream);
+}
+
+AIB_API int aib_decode_gemv_bf16_batch(const aib_gemv_desc *descs, int count, int32_t *d_status, void *stream) {
+  return gemv_launch(descs, count, d_status, stream);
 }
 
 AIB_API int aib_recombine(const uint8_t *exponent, const uint8_t *sign_mantissa, int64_t n, uint16_t *out,

@@ -446,6 +446,20 @@ class TPDecoder:
             st.graph.replay()
         return torch.cat([ids, first.reshape(1, 1), st.tokens[:max_new_tokens - 1].reshape(1, -1)], 1)
 
+    @torch.no_grad()
+    def replay_steps(self, n: int) -> int:
+        """Replays the captured single-token step up to n more times,
+        continuing the last graphed generation (for timing the step alone);
+        returns how many ran (bounded by the static cache length)."""
+        st = self._graph_state
+        if st is None or st.graph is None:
+            raise RuntimeError("no captured step: call generate_greedy_graphed first")
+        used = int(st.pos.item())
+        k = max(0, min(n, st.max_len - used, st.max_len - int(st.step.item())))
+        for _ in range(k):
+            st.graph.replay()
+        return k
+
     def release_graphs(self) -> None:
         """Drops the captured step (release before destroying the process group)."""
         self._graph_state = None

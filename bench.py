@@ -44,7 +44,12 @@ QWEN3_14B_LAYER = [("q_proj", 5120, 5120), ("k_proj", 1024, 5120), ("v_proj", 10
                    ("o_proj", 5120, 5120), ("gate_proj", 17408, 5120), ("up_proj", 17408, 5120),
                    ("down_proj", 5120, 17408)]
 CONFIG1 = [("w", 4096, 4096)]
-WORKLOADS = {"qwen3-14b-layer": QWEN3_14B_LAYER, "config1-4096x4096": CONFIG1}
+WORKLOADS = {"qwen3-14b-layer": QWEN3_14B_LAYER, "config1-4096x4096": CONFIG1,
+             "qwen3-14b-layer-tp8": QWEN3_14B_LAYER}
+# per-tensor chunk sizes where a workload differs from the reference default
+# (a store written with write_store(tp_row_chunks=8): row-parallel tensors in
+# whole chunks of every rank's columns)
+WORKLOAD_CHUNKS = {"qwen3-14b-layer-tp8": {"o_proj": 640, "down_proj": 1088}}
 FAST_TABLE_BYTES = 4096 * 8
 # BASELINE configs 2 and 4 (Qwen3 0.6B / 14B shapes), random-init weights
 QWEN3_06B = dict(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
@@ -73,13 +78,13 @@ def algorithmic_bytes(layers) -> int:
     return total
 
 
-def make_layers(spec, seed: int, device):
+def make_layers(spec, seed: int, device, chunks: dict | None = None):
     from afterimage_b200.runtime.compressed_store import compress_layer
     g = torch.Generator(device=device).manual_seed(seed)
     out = []
-    for i, (_, rows, cols) in enumerate(spec):
+    for i, (name, rows, cols) in enumerate(spec):
         W = (torch.randn(rows, cols, generator=g, device=device) * 0.02).to(torch.bfloat16)
-        out.append(compress_layer(W.cpu(), chunk_size=1024))
+        out.append(compress_layer(W.cpu(), chunk_size=(chunks or {}).get(name, 1024)))
         del W
     return out
 
@@ -417,9 +422,19 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
                 b.record()
                 torch.cuda.synchronize()
                 gms = _max_over_ranks(a.elapsed_time(b), world, dev)
+                # the captured step alone (prefill excluded): 32 more replays
+                _barrier(world)
+                a.record()
+                k = dec.replay_steps(32)
+                b.record()
+                torch.cuda.synchronize()
+                sms = _max_over_ranks(a.elapsed_time(b) / max(k, 1), world, dev)
                 info["graphed"] = {"tokens_per_s": round(args.new_tokens / (gms / 1e3), 3),
                                    "s_per_token": round(gms / 1e3 / args.new_tokens, 4),
-                                   "tokens_equal_eager": bool(torch.equal(gseq.cpu(), seqs[name]))}
+                                   "tokens_equal_eager": bool(torch.equal(gseq.cpu(), seqs[name])),
+                                   "step_ms": round(sms, 3), "step_tokens_per_s": round(1e3 / sms, 2),
+                                   "note": "tokens_per_s includes the eager 64-token prefill; step_ms is one "
+                                           "replay of the captured single-token step"}
                 dec.release_graphs()
             if resident == "streamed":
                 hb = dec.h2d_bytes_per_forward()
@@ -458,7 +473,7 @@ def run_reference(args, world, rank):
         return 0
     spec = WORKLOADS[args.workload]
     dev = "cuda" if torch.cuda.is_available() else "cpu"
-    layers = make_layers(spec, 1234, dev)
+    layers = make_layers(spec, 1234, dev, WORKLOAD_CHUNKS.get(args.workload))
     nbytes = algorithmic_bytes(layers)
     from oracle import oracle as O
     threads = O.max_threads()
@@ -520,7 +535,8 @@ def main(argv=None) -> int:
     from afterimage_b200.runtime import _device
 
     spec = WORKLOADS[args.workload]
-    host_layers = [make_layers(spec, 1000 * rank + i + 1, dev) for i in range(args.layers)]
+    host_layers = [make_layers(spec, 1000 * rank + i + 1, dev, WORKLOAD_CHUNKS.get(args.workload))
+                   for i in range(args.layers)]
     resident = [[LD.upload_layer(t, dev) for t in layer] for layer in host_layers]
     outs = [torch.empty(r, c, dtype=torch.bfloat16, device=dev) for _, r, c in spec]
     decoder = LD.LayerDecoder(dev)
@@ -628,7 +644,8 @@ def main(argv=None) -> int:
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
             "data": "synthetic: random N(0,0.02) BF16 weights, seeded, encoded by afterimage_b200 (reference-identical)",
             "config": {"workload": args.workload, "tensors": [n for n, _, _ in spec],
-                       "layer_weights": sum(r * c for _, r, c in spec), "chunk_size": 1024,
+                       "layer_weights": sum(r * c for _, r, c in spec),
+                       "chunk_size": {"default": 1024, **WORKLOAD_CHUNKS.get(args.workload, {})},
                        "distinct_resident_layers": args.layers, "l2": "inputs > L2 (no flush needed)",
                        "algorithmic_bytes_per_step": int(step_bytes[0]), "parallelism": f"replica{world}"},
             "gpu_launches": args.steps * (-(-len(spec) // 16)),

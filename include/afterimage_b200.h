@@ -135,6 +135,30 @@ int aib_decode_exponents_i32(const aib_stream_desc *desc, int32_t *d_status, voi
 #define AIB_MAX_BATCH 16
 int aib_decode_bf16_batch(const aib_stream_desc *descs, int count, int32_t *d_status, void *stream);
 
+/* Fused decode -> GEMV for one input vector (a single-token projection):
+ * y = W x with W given only in compressed form. `stream` describes the
+ * tensor as for the decode; its element range must be whole rows of the
+ * row-major [rows, cols] matrix (elem_begin and elem_end multiples of
+ * cols), cols a multiple of chunk_size, chunk_size a multiple of 16,
+ * sign_mantissa 16-byte aligned;
+ * stream.out is ignored. Replaces, for M = 1, the decode followed by the
+ * consuming nn.Linear / F.linear on the decoded weights
+ * (afterimage/runtime/streaming_engine.py:1871-1915 layer hooks around the
+ * transformers decoder layer; the chunked head's F.linear, :2330). */
+typedef struct aib_gemv_desc {
+  aib_stream_desc stream;
+  int64_t cols;       /* row length */
+  const void *x;      /* device bf16[cols], 8-byte aligned */
+  float *partial;     /* device scratch: (elem_end - elem_begin) / chunk_size floats */
+  void *y;            /* device bf16[(elem_end - elem_begin) / cols] */
+} aib_gemv_desc;
+
+/* Up to AIB_MAX_BATCH GEMVs (each with its own x) in one launch pair: the
+ * decode-and-multiply kernel writes one fp32 partial per chunk, a second
+ * kernel sums each row's partials in column order and rounds to BF16
+ * (deterministic). Work is enqueued on `stream`; no synchronisation. */
+int aib_decode_gemv_bf16_batch(const aib_gemv_desc *descs, int count, int32_t *d_status, void *stream);
+
 /* Elementwise recombine of an already-decoded exponent field: replaces
  * recombine_exponent_and_sign_mantissa / _recombine
  * (afterimage/runtime/compressed_store.py:94-130). */

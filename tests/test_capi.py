@@ -39,21 +39,22 @@ def test_library_exports_nothing_else():
     assert extra == [], extra[:20]
 
 
-def test_descriptor_layout_matches_header_order(tmp_path):
-    """ctypes' aib_stream_desc must have the C compiler's field offsets."""
+@pytest.mark.parametrize("ctype,cname", [(_lib.StreamDesc, "aib_stream_desc"), (_lib.GemvDesc, "aib_gemv_desc")])
+def test_descriptor_layout_matches_header_order(tmp_path, ctype, cname):
+    """The ctypes descriptors must have the C compiler's size and field offsets."""
     import subprocess
-    fields = [f for f, _ in _lib.StreamDesc._fields_]
+    fields = [f for f, _ in ctype._fields_]
     src = tmp_path / "layout.c"
     src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"afterimage_b200.h\"\n"
-                   "int main(void){printf(\"%zu\\n\", sizeof(aib_stream_desc));"
-                   + "".join('printf("%%zu\\n", offsetof(aib_stream_desc, %s));' % f for f in fields)
+                   "int main(void){printf(\"%%zu\\n\", sizeof(%s));" % cname
+                   + "".join('printf("%%zu\\n", offsetof(%s, %s));' % (cname, f) for f in fields)
                    + "return 0;}\n")
     exe = tmp_path / "layout"
     subprocess.run(["gcc", "-I", str(HEADER.parent), str(src), "-o", str(exe)], check=True)
     got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True,
                                           check=True).stdout.split()]
-    assert got[0] == ctypes.sizeof(_lib.StreamDesc)
-    assert got[1:] == [getattr(_lib.StreamDesc, f).offset for f in fields]
+    assert got[0] == ctypes.sizeof(ctype)
+    assert got[1:] == [getattr(ctype, f).offset for f in fields]
 
 
 def test_host_validation_rejects_bad_descriptors_without_a_gpu():
@@ -77,6 +78,46 @@ def test_host_validation_rejects_bad_descriptors_without_a_gpu():
     assert L.aib_decode_exponents_u8(ctypes.byref(d), None, None) == _lib.AIB_OK
     assert L.aib_decode_bf16_batch(ctypes.byref(d), 0, None, None) == _lib.AIB_EINVAL
     assert L.aib_decode_bf16_batch(ctypes.byref(d), 17, None, None) == _lib.AIB_EINVAL
+
+
+def test_gemv_host_validation_without_a_gpu():
+    """Every argument check of the fused decode-GEMV runs on the host."""
+    L = _lib.load()
+    g = _lib.GemvDesc()
+    d = g.stream
+    assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 0, None, None) == _lib.AIB_EINVAL
+    # no rows: nothing to check or do
+    assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_OK
+    d.n_symbols, d.elem_end = 64, 64
+    assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL
+    assert b"null x" in L.aib_last_error()
+    g.x, g.partial, g.y = 0x1000, 0x2000, 0x3000
+    g.x = 0x1004
+    assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL
+    assert b"aligned" in L.aib_last_error()
+    g.x = 0x1000
+    d.chunk_size = 6
+    assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL
+    assert b"multiple of 16" in L.aib_last_error()
+    d.chunk_size = 64
+    g.cols = 100
+    assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL
+    assert b"cols" in L.aib_last_error()
+    g.cols = 128
+    d.n_symbols, d.elem_begin, d.elem_end = 512, 64, 512
+    assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL
+    assert b"whole rows" in L.aib_last_error()
+    d.elem_begin = 128
+    assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL
+    assert b"sign_mantissa" in L.aib_last_error()
+    d.sign_mantissa = 0x4000
+    d.max_bits = 8
+    # the shared stream checks follow (null packed here)
+    assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL
+    assert b"packed" in L.aib_last_error()
+    # an empty range needs no device
+    d.elem_begin = d.elem_end = 256
+    assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_OK
 
 
 def test_tables_bytes_and_abi_version():

@@ -290,7 +290,11 @@ def test_bad_descriptor_rejected_on_host():
 
 # --- direct C-ABI use: batch of tensors in one launch ---
 
-def test_batch_entry_point_decodes_several_tensors_in_one_launch():
+@pytest.mark.parametrize("sizes", [(1024, 1024, 1024, 7, 1024),      # mixed: per-job loop choice
+                                   (1024,) * 5,                       # all default: specialised loop
+                                   (640, 1088, 64, 7, 2176),          # none default: general loop
+                                   (1024, 640, 1024, 1088, 1024)])    # a TP-ready layer's mix
+def test_batch_entry_point_decodes_several_tensors_in_one_launch(sizes):
     from afterimage_b200 import _lib
     from afterimage_b200.runtime import _device
     from afterimage_b200.runtime.compressed_store import compress_layer
@@ -301,7 +305,7 @@ def test_batch_entry_point_decodes_several_tensors_in_one_launch():
     for i, s in enumerate(shapes):
         g = torch.Generator().manual_seed(i)
         W = (torch.randn(*s, generator=g) * (0.02 * (i + 1))).to(torch.bfloat16)
-        layer = compress_layer(W, chunk_size=1024 if i != 3 else 7)
+        layer = compress_layer(W, chunk_size=sizes[i])
         t = prepare_decode_tables(layer.encoded, dev)
         ds = _device.upload_stream(layer.encoded, dev)
         sm = layer.sign_mantissa.to(dev)
