@@ -21,6 +21,7 @@ AIB_OK = 0
 AIB_EINVAL = 1
 AIB_ECUDA = 2
 AIB_MAX_BATCH = 16
+AIB_GEMV_SCRATCH_FLOATS = 1 << 20
 
 STATUS_BAD_CHUNK_RANGE = 1
 STATUS_LUT_NOT_PREFIX = 2
@@ -87,6 +88,7 @@ SIGNATURES = [
     ("aib_decode_exponents_i32", CI, [ctypes.POINTER(StreamDesc), P, P]),
     ("aib_decode_bf16_batch", CI, [ctypes.POINTER(StreamDesc), CI, P, P]),
     ("aib_decode_gemv_bf16_batch", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
+    ("aib_decode_gemv_bf16_batch_noalloc", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
     ("aib_recombine", CI, [P, P, I64, P, P]),
 ]
 

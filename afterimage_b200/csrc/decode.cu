@@ -1208,6 +1208,48 @@ AIB_API int aib_decode_gemv_bf16_batch(const aib_gemv_desc *descs, int count, in
   return gemv_launch(descs, count, d_status, stream);
 }
 
+// Library-owned scratch for aib_decode_gemv_bf16_batch_noalloc: callers that
+// only hold device pointers handed to them (no allocator of their own) get
+// the per-chunk partial sums placed here. One array per device context,
+// shared by all such calls, so they must be stream-ordered.
+static __device__ __align__(256) float g_gemv_scratch[AIB_GEMV_SCRATCH_FLOATS];
+
+AIB_API int aib_decode_gemv_bf16_batch_noalloc(const aib_gemv_desc *descs, int count, int32_t *d_status,
+                                               void *stream) {
+  if (count < 1 || count > AIB_MAX_BATCH) {
+    aib_set_errorf("batch count must be in [1, %d], got %d", AIB_MAX_BATCH, count);
+    return AIB_EINVAL;
+  }
+  if (!descs) return aib_set_error("null descriptor array"), AIB_EINVAL;
+  // the scratch each descriptor needs, checked before any device call
+  int64_t need[AIB_MAX_BATCH];
+  int64_t total = 0;
+  for (int i = 0; i < count; ++i) {
+    const aib_stream_desc &d = descs[i].stream;
+    if (d.chunk_size < 1) return aib_set_errorf("chunk_size must be >= 1, got %d", d.chunk_size), AIB_EINVAL;
+    if (d.elem_begin < 0 || d.elem_end < d.elem_begin)
+      return aib_set_error("gemv: bad element range"), AIB_EINVAL;
+    need[i] = (d.elem_end - d.elem_begin + d.chunk_size - 1) / d.chunk_size;
+    total += need[i];
+  }
+  if (total > AIB_GEMV_SCRATCH_FLOATS)
+    return aib_set_errorf("gemv: the batch needs %lld scratch floats, the library holds %d", (long long)total,
+                          AIB_GEMV_SCRATCH_FLOATS),
+           AIB_EINVAL;
+  float *base = nullptr;
+  AIB_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&base), g_gemv_scratch));
+  aib_gemv_desc local[AIB_MAX_BATCH];
+  int64_t off = 0;
+  for (int i = 0; i < count; ++i) {
+    local[i] = descs[i];
+    local[i].partial = base + off;
+    off += (need[i] + 63) / 64 * 64;  // keep each descriptor's area 256-byte aligned
+  }
+  if (off > AIB_GEMV_SCRATCH_FLOATS)
+    return aib_set_error("gemv: the batch's aligned scratch areas do not fit"), AIB_EINVAL;
+  return gemv_launch(local, count, d_status, stream);
+}
+
 AIB_API int aib_recombine(const uint8_t *exponent, const uint8_t *sign_mantissa, int64_t n, uint16_t *out,
                           void *stream) {
   if (n < 0) return aib_set_error("aib_recombine: negative n"), AIB_EINVAL;

@@ -159,6 +159,20 @@ typedef struct aib_gemv_desc {
  * (deterministic). Work is enqueued on `stream`; no synchronisation. */
 int aib_decode_gemv_bf16_batch(const aib_gemv_desc *descs, int count, int32_t *d_status, void *stream);
 
+/* The same fused decode -> GEMV with no caller scratch: the per-chunk
+ * partial sums go to a fixed device array inside the library
+ * (AIB_GEMV_SCRATCH_FLOATS floats for the whole batch; descs[i].partial is
+ * ignored). For callers that receive the tensor, x and y as device pointers
+ * from someone else and have no device allocator of their own -- a binding
+ * from a host language over this C ABI that is handed buffers by another
+ * framework, for example. The array is shared by every call of the process
+ * on the device, so calls must be ordered on one stream (two such calls
+ * running concurrently on different streams would overwrite each other's
+ * partial sums). A batch that needs more scratch returns AIB_EINVAL before
+ * touching the device. */
+#define AIB_GEMV_SCRATCH_FLOATS (1 << 20)
+int aib_decode_gemv_bf16_batch_noalloc(const aib_gemv_desc *descs, int count, int32_t *d_status, void *stream);
+
 /* Elementwise recombine of an already-decoded exponent field: replaces
  * recombine_exponent_and_sign_mantissa / _recombine
  * (afterimage/runtime/compressed_store.py:94-130). */
