@@ -673,6 +673,7 @@ struct GemvJob {
   int64_t rows;
   int64_t n_groups;      // ceil(rows / 32) * cpr
   int64_t row_begin;     // rows of the batch's earlier jobs
+  int64_t cols;
   int32_t cpr;           // chunks per row
   int32_t chunk_size;
   int32_t max_bits;
@@ -688,25 +689,12 @@ struct GemvBatch {
 
 constexpr int kGemvSmemBytes = kFastBytes + kThreads * kSlotRow;
 
-// Sign/mantissa bytes of a lane's chunk, read 16 at a time two blocks ahead
-// of use (register queue: `cur` holds symbols [kb, kb + 16), `nxt` the 16
-// after), so the word multiply never waits on a global load.
-struct SmQueue {
-  uint4 cur, nxt;
-  int kb;
-};
-
-__device__ __forceinline__ uint4 ldg16(const uint8_t *p) { return __ldg(reinterpret_cast<const uint4 *>(p)); }
-
-__device__ __forceinline__ void smq_init(SmQueue &q, const uint8_t *smp, int need) {
-  q.cur = need > 0 ? ldg16(smp) : make_uint4(0, 0, 0, 0);
-  q.nxt = need > 16 ? ldg16(smp + 16) : make_uint4(0, 0, 0, 0);
-  q.kb = 0;
-}
-
-// four weights (exponent bytes of `ew`, sign/mantissa word `sw`) times
-// x[k..k+3], accumulated in fp32
-__device__ __forceinline__ void dot4(uint32_t ew, uint32_t sw, int k, const uint16_t *xp, float &a0, float &a1) {
+// four weights (exponent bytes of `ew`, sign/mantissa bytes smp[k..k+3])
+// times x[k..k+3] (bf16, read through L1: every lane of the warp is at
+// about the same column), accumulated in fp32
+__device__ __forceinline__ void dot4(uint32_t ew, int k, const uint8_t *smp, const uint16_t *xp, float &a0,
+                                     float &a1) {
+  const uint32_t sw = __ldg(reinterpret_cast<const unsigned int *>(smp + k));
   const uint2 xv = __ldg(reinterpret_cast<const uint2 *>(xp + k));
   const uint32_t M = 0x807F807Fu;
   const uint32_t p01 = __byte_perm(ew, 0, 0x4140) * 128u + (__byte_perm(sw, 0, 0x1100) & M);
@@ -720,22 +708,12 @@ __device__ __forceinline__ void dot4(uint32_t ew, uint32_t sw, int k, const uint
 // emit() for the GEMV: a full word of four symbols is multiplied in at once
 // (only words inside the chunk: need is a multiple of four)
 __device__ __forceinline__ void emit_dot(uint2 e, uint32_t &olo, uint32_t &ohi, int &n8, int &k, int need,
-                                         SmQueue &q, const uint8_t *smp, const uint16_t *xp, float &a0,
-                                         float &a1) {
+                                         const uint8_t *smp, const uint16_t *xp, float &a0, float &a1) {
   olo |= e.x << n8;
   ohi |= __funnelshift_l(e.x, 0u, static_cast<uint32_t>(n8));
   n8 += static_cast<int>(e.y >> 8);
   if (n8 >= 32) {
-    if (k < need) {
-      const int w = (k >> 2) & 3;
-      const uint32_t sw = w == 0 ? q.cur.x : (w == 1 ? q.cur.y : (w == 2 ? q.cur.z : q.cur.w));
-      dot4(olo, sw, k, xp, a0, a1);
-      if (w == 3) {
-        q.cur = q.nxt;
-        q.kb += 16;
-        if (q.kb + 16 < need) q.nxt = ldg16(smp + q.kb + 16);
-      }
-    }
+    if (k < need) dot4(olo, k, smp, xp, a0, a1);
     olo = ohi;
     ohi = 0;
     n8 -= 32;
@@ -781,8 +759,6 @@ __device__ __forceinline__ void gemv_groups(const GemvJob &G, const uint2 *s_fas
     int k = 0, n8 = 0;
     uint32_t olo = 0, ohi = 0;
     float a0 = 0.f, a1 = 0.f;
-    SmQueue q;
-    smq_init(q, smp, need);
     while (__any_sync(0xffffffffu, k < need)) {
       if (k < need) {
         if (rd.nb < 32) reader_refill(rd, my_stream, src, bmax, pol_keep);
@@ -792,7 +768,7 @@ __device__ __forceinline__ void gemv_groups(const GemvJob &G, const uint2 *s_fas
           const uint2 e = s_fast[rd.ah >> (32 - kFastBits)];
           ymin = min(ymin, e.y);
           reader_consume(rd, e.y & 31u);
-          emit_dot(e, olo, ohi, n8, k, need, q, smp, xp, a0, a1);
+          emit_dot(e, olo, ohi, n8, k, need, smp, xp, a0, a1);
         }
         if (__any_sync(__activemask(), ymin == 0u)) {
           if (ymin == 0u) {
@@ -801,7 +777,7 @@ __device__ __forceinline__ void gemv_groups(const GemvJob &G, const uint2 *s_fas
             const uint32_t sy = static_cast<uint32_t>(__ldg(G.sym_lut + w)) & 0xFFu;
             const uint32_t l = static_cast<uint32_t>(static_cast<int>(__ldg(G.len_lut + w))) & 31u;
             reader_consume(rd, l);
-            emit_dot(make_uint2(sy, 8u << 8), olo, ohi, n8, k, need, q, smp, xp, a0, a1);
+            emit_dot(make_uint2(sy, 8u << 8), olo, ohi, n8, k, need, smp, xp, a0, a1);
           }
         }
       }
@@ -1070,16 +1046,16 @@ static int gemv_launch(const aib_gemv_desc *descs, int count, int32_t *status, v
     if (!g->x || !g->partial || !g->y) return aib_set_error("gemv: null x, partial or y"), AIB_EINVAL;
     if (!aligned(g->x, 8) || !aligned(g->partial, 4) || !aligned(g->y, 2))
       return aib_set_error("gemv: x must be 8-byte, partial 4-byte and y 2-byte aligned"), AIB_EINVAL;
-    if (d.chunk_size < 16 || d.chunk_size % 16)
-      return aib_set_errorf("gemv: chunk_size must be a positive multiple of 16, got %d", d.chunk_size), AIB_EINVAL;
+    if (d.chunk_size < 4 || d.chunk_size % 4)
+      return aib_set_errorf("gemv: chunk_size must be a positive multiple of 4, got %d", d.chunk_size), AIB_EINVAL;
     if (g->cols < 1 || g->cols % d.chunk_size)
       return aib_set_errorf("gemv: cols %lld must be a positive multiple of chunk_size %d", (long long)g->cols,
                             d.chunk_size),
              AIB_EINVAL;
     if (d.elem_begin % g->cols || d.elem_end % g->cols)
       return aib_set_error("gemv: the element range must be whole rows"), AIB_EINVAL;
-    if (!d.sign_mantissa || !aligned(d.sign_mantissa, 16))
-      return aib_set_error("gemv: sign_mantissa must be a 16-byte aligned device pointer"), AIB_EINVAL;
+    if (!d.sign_mantissa || !aligned(d.sign_mantissa, 4))
+      return aib_set_error("gemv: sign_mantissa must be a 4-byte aligned device pointer"), AIB_EINVAL;
     // the stream checks shared with the decode (out is not written here)
     aib_stream_desc copy = d;
     copy.out = g->y;
@@ -1106,6 +1082,7 @@ static int gemv_launch(const aib_gemv_desc *descs, int count, int32_t *status, v
     G.y = static_cast<uint16_t *>(g->y);
     G.c0 = d.elem_begin / d.chunk_size;
     G.rows = (d.elem_end - d.elem_begin) / g->cols;
+    G.cols = g->cols;
     G.cpr = static_cast<int32_t>(g->cols / d.chunk_size);
     G.n_groups = (G.rows + 31) / 32 * G.cpr;
     G.row_begin = total_rows;

@@ -12,8 +12,8 @@ kernel sums every row's partials in column order (deterministic), rounding
 to BF16 like F.linear's output.
 
 Requirements (checked by the library): the element range is whole rows,
-the row length is a multiple of chunk_size, chunk_size is a multiple of 16
-and the sign/mantissa bytes are 16-byte aligned.
+the row length is a multiple of chunk_size, chunk_size is a multiple of 4
+and the sign/mantissa bytes are 4-byte aligned.
 """
 from __future__ import annotations
 
@@ -25,7 +25,7 @@ from . import _device
 
 def gemv_supported(enc, cols: int, e0: int = 0) -> bool:
     cs = int(enc.chunk_size)
-    return cs >= 16 and cs % 16 == 0 and cols % cs == 0 and e0 % cols == 0
+    return cs >= 4 and cs % 4 == 0 and cols % cs == 0 and e0 % cols == 0
 
 
 def gemv_desc(ds: _device.DeviceStream, tables, enc, e0: int, e1: int, sign_mantissa: torch.Tensor, cols: int,

@@ -139,8 +139,8 @@ int aib_decode_bf16_batch(const aib_stream_desc *descs, int count, int32_t *d_st
  * y = W x with W given only in compressed form. `stream` describes the
  * tensor as for the decode; its element range must be whole rows of the
  * row-major [rows, cols] matrix (elem_begin and elem_end multiples of
- * cols), cols a multiple of chunk_size, chunk_size a multiple of 16,
- * sign_mantissa 16-byte aligned;
+ * cols), cols a multiple of chunk_size, chunk_size a multiple of 4,
+ * sign_mantissa 4-byte aligned;
  * stream.out is ignored. Replaces, for M = 1, the decode followed by the
  * consuming nn.Linear / F.linear on the decoded weights
  * (afterimage/runtime/streaming_engine.py:1871-1915 layer hooks around the

@@ -98,7 +98,7 @@ def test_gemv_host_validation_without_a_gpu():
     g.x = 0x1000
     d.chunk_size = 6
     assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL
-    assert b"multiple of 16" in L.aib_last_error()
+    assert b"multiple of 4" in L.aib_last_error()
     d.chunk_size = 64
     g.cols = 100
     assert L.aib_decode_gemv_bf16_batch(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL

@@ -33,7 +33,7 @@ def _close(y, ref, mag):
 
 
 @pytest.mark.parametrize("shape,cs", [((1024, 4096), 1024), ((512, 5120), 1024), ((640, 1280), 640),
-                                      ((256, 2176), 1088), ((300, 256), 64), ((33, 96), 16), ((64, 1024), 1024)])
+                                      ((256, 2176), 1088), ((300, 256), 64), ((33, 96), 4), ((64, 1024), 1024), ((40, 32768), 1024)])
 def test_gemv_matches_float64_reference(shape, cs):
     g = torch.Generator().manual_seed(shape[0] + cs)
     W = (torch.randn(*shape, generator=g) * 0.02).to(torch.bfloat16)
