@@ -95,12 +95,35 @@ class PinnedBuffer:
         return self._t
 
 
-class BinaryWeightReader:
-    """One open file handle for the store's lifetime."""
+_POOLS: dict = {}
+_POOLS_LOCK = __import__("threading").Lock()
 
-    def __init__(self, path, direct: bool = False):
+
+def _pool(threads: int):
+    """Process-wide reader pool (threads release the GIL inside preadv)."""
+    import concurrent.futures
+    with _POOLS_LOCK:
+        pool = _POOLS.get(threads)
+        if pool is None:
+            pool = concurrent.futures.ThreadPoolExecutor(max_workers=threads, thread_name_prefix="aib-read")
+            _POOLS[threads] = pool
+        return pool
+
+
+class BinaryWeightReader:
+    """One open file handle for the store's lifetime.
+
+    `threads` > 1 splits the pinned reads of `read_many` into pieces of at
+    least `piece_bytes` read concurrently with positional reads (one
+    thread's page-cache copy rate is a few GB/s; a PCIe 5 link takes
+    ~55 GB/s)."""
+
+    def __init__(self, path, direct: bool = False, threads: int = 1, piece_bytes: int = 8 << 20):
         self.path = pathlib.Path(path)
         self._fh = open(self.path, "rb")
+        self._fd = self._fh.fileno()
+        self.threads = max(1, int(threads))
+        self.piece_bytes = max(_DIRECT_ALIGN, int(piece_bytes) // _DIRECT_ALIGN * _DIRECT_ALIGN)
         self._direct_fd = None
         if direct and hasattr(os, "O_DIRECT"):
             try:
@@ -121,25 +144,50 @@ class BinaryWeightReader:
                 raise _checksum_error(ref, got)
         return np.frombuffer(data, dtype=ref["dtype"]).copy().reshape(ref["shape"])
 
+    def _pread_full(self, fd: int, start: int, view: memoryview) -> int:
+        got = 0
+        n = len(view)
+        while got < n:
+            k = os.preadv(fd, [view[got:]], start + got)
+            if k <= 0:
+                break
+            got += k
+        return got
+
+    def _readinto_parallel(self, start: int, view: memoryview, direct: bool) -> int:
+        """Fills `view` from [start, start + len(view)) in pieces on the
+        reader pool; returns the bytes read (short only at end of file)."""
+        n = len(view)
+        step = self.piece_bytes
+        fd = self._direct_fd if direct else self._fd
+        jobs = [(o, min(step, n - o)) for o in range(0, n, step)]
+        futs = [_pool(self.threads).submit(self._pread_full, fd, start + o, view[o:o + m]) for o, m in jobs]
+        got = [f.result() for f in futs]
+        total = 0
+        for (o, m), g in zip(jobs, got):
+            total += g
+            if g < m:
+                return total
+        return total
+
     def _readinto(self, start: int, view: memoryview) -> int:
         """Fill `view` with file bytes [start, start + len(view)). O_DIRECT
         when enabled and the destination/offset/length are sector aligned
         (retrying buffered on EINVAL); buffered otherwise."""
         n = len(view)
+        parallel = self.threads > 1 and n > self.piece_bytes
         if self._direct_fd is not None and n and start % _DIRECT_ALIGN == 0:
             addr = np.frombuffer(view, dtype=np.uint8).ctypes.data
             if addr % _DIRECT_ALIGN == 0:
                 try:
-                    got = 0
-                    while got < n:
-                        k = os.preadv(self._direct_fd, [view[got:]], start + got)
-                        if k <= 0:
-                            break
-                        got += k
-                    return got
+                    if parallel:
+                        return self._readinto_parallel(start, view, True)
+                    return self._pread_full(self._direct_fd, start, view)
                 except OSError:
                     os.close(self._direct_fd)
                     self._direct_fd = None
+        if parallel:
+            return self._readinto_parallel(start, view, False)
         self._fh.seek(start)
         return self._fh.readinto(view)
 

@@ -64,6 +64,7 @@ class EngineConfig:
     ram_tier_format: str = "decoded"        # "decoded" | "compressed"
     vram_tier_format: str = "decoded"       # "decoded" | "compressed" (decoded per use from HBM)
     io_prefetch_depth: int = 1
+    io_threads: int = 8                     # concurrent positional reads of the pinned prefetch slots
     storage_extent_max_gap_bytes: int = 0
     storage_extent_max_bytes: int = 1 << 28
     direct_io: bool = False
@@ -80,6 +81,8 @@ class EngineConfig:
             raise ValueError("decode_slice_elems must be positive")
         if self.io_prefetch_depth < 0:
             raise ValueError("io_prefetch_depth must be >= 0")
+        if self.io_threads < 1:
+            raise ValueError("io_threads must be >= 1")
         if self.ram_tier_format not in ("decoded", "compressed"):
             raise ValueError("ram_tier_format must be 'decoded' or 'compressed'")
         if self.vram_tier_format not in ("decoded", "compressed"):
@@ -398,7 +401,8 @@ class StreamingLosslessModel:
         self._prefetch = depth > 0
         self._slots = [PinnedBuffer() for _ in range(depth + 1)] if self._prefetch else [PinnedBuffer()]
         self._slot_free = [None] * len(self._slots)          # CUDA event: H2D from the slot finished
-        self._slot_readers = [BinaryWeightReader(self.store / "weights.bin", direct=self.config.direct_io)
+        self._slot_readers = [BinaryWeightReader(self.store / "weights.bin", direct=self.config.direct_io,
+                                                 threads=self.config.io_threads)
                               for _ in self._slots]
         self._pool = concurrent.futures.ThreadPoolExecutor(max_workers=max(1, depth), thread_name_prefix="aib-io")
         self._futures: dict[int, concurrent.futures.Future] = {}

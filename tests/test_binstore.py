@@ -47,6 +47,30 @@ def test_read_many_coalesces_bit_exact_in_any_mode(tmp_path, pinned, direct):
     assert all(np.array_equal(a, b) for a, b in zip(got, arrays))
 
 
+@pytest.mark.parametrize("direct", [False, True])
+@pytest.mark.parametrize("threads,piece", [(4, 4096), (3, 12288), (8, 1 << 20)])
+def test_parallel_pinned_reads_are_bit_exact(tmp_path, direct, threads, piece):
+    """Extents split into pieces read concurrently land exactly where a
+    single sequential read puts them (ragged last piece, unaligned blob
+    starts inside extents, several extents)."""
+    rng = np.random.default_rng(threads + piece)
+    arrays = [rng.integers(0, 256, n, dtype=np.uint8) for n in (5, 70001, 4096, 123457, 3, 65536 * 3 + 17)]
+    refs = _store(tmp_path / "w.bin", arrays)
+    with BinaryWeightReader(tmp_path / "w.bin", direct=direct, threads=threads, piece_bytes=piece) as r:
+        for extent in (1 << 30, 100000):
+            got, calls, nbytes = r.read_many(refs, max_extent_bytes=extent, pinned=True)
+            assert all(np.array_equal(a, b) for a, b in zip(got, arrays))
+            assert nbytes == sum(a.nbytes for a in arrays)
+
+
+def test_parallel_short_read_raises(tmp_path):
+    refs = _store(tmp_path / "w.bin", [np.zeros(50000, np.uint8)])
+    bad = dict(refs[0], nbytes=90000, shape=[90000])
+    with BinaryWeightReader(tmp_path / "w.bin", threads=4, piece_bytes=4096) as r:
+        with pytest.raises(ValueError, match="short read"):
+            r.read_many([bad], pinned=True)
+
+
 def test_read_many_respects_extent_bound_and_original_order(tmp_path):
     arrays = [np.full(32, v, dtype=np.uint8) for v in range(3)]
     refs = _store(tmp_path / "w.bin", arrays)
