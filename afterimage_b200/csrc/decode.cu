@@ -309,42 +309,39 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 // Per-lane bit reader over one chunk: a 64-bit MSB-aligned buffer held as
-// two 32-bit halves (ah:al) with `nb` valid bits, fed 32 bits at a time
-// from the current 16-byte block (big-endian words q0..q3, `qn` left).
-// Every shift amount is known to be below 32 (consumption <= 16 bits per
-// lookup, refills while nb < 32), so each step is a single funnel shift.
-// Blocks stream through a per-lane shared-memory ring of kSlots 16-byte
-// slots: kSlots - 1 copies are always in flight, so a block is requested
-// ~(kSlots - 1) * 16 bytes before the lane reaches it.
+// two 32-bit halves (ah:al) with `nb` valid bits, refilled 32 bits at a time
+// straight from the lane's shared-memory stream ring (word `wi`, counted
+// from the 16-byte block that holds the chunk's first byte). Every shift
+// amount is below 32 (consumption <= 16 bits per lookup, refills while
+// nb < 32), so each step is a single funnel shift. The ring has kSlots
+// 16-byte slots, block k in slot k % kSlots; entering block k waits for its
+// copy and requests block k + kSlots - 1 into the slot block k - 1 used, so
+// kSlots - 1 copies stay in flight ~(kSlots - 1) * 16 bytes ahead.
 struct Reader {
   uint32_t ah, al;
   int nb;
-  uint32_t q0, q1, q2, q3;
-  int qn;
-  int slot;    // slot holding the next block to consume
+  int wi;      // next word to load (block wi / 4, slot (wi / 4) % kSlots)
   int64_t bi;  // next 16-byte block to request
 };
 
+// entering the block of word wi: its copy has landed; request the one
+// kSlots - 1 blocks ahead
 __device__ __forceinline__ void reader_next_block(Reader &r, unsigned char *ring, const uint4 *src, int64_t bmax,
                                                   uint64_t pol) {
-  cp_async_wait<kSlots - 2>();  // the oldest outstanding copy is the block needed now
-  const uint4 b = *reinterpret_cast<const uint4 *>(ring + r.slot * 16);
-  r.q0 = bswap(b.x); r.q1 = bswap(b.y); r.q2 = bswap(b.z); r.q3 = bswap(b.w);
-  r.qn = 4;
-  // block bi belongs in the slot drained by the previous call: slot (slot - 1)
-  cp_async16(ring + ((r.slot + kSlots - 1) & (kSlots - 1)) * 16, src + min(r.bi, bmax), pol);
+  cp_async_wait<kSlots - 2>();
+  cp_async16(ring + (((r.wi >> 2) + kSlots - 1) & (kSlots - 1)) * 16, src + min(r.bi, bmax), pol);
   ++r.bi;
-  r.slot = (r.slot + 1) & (kSlots - 1);
 }
 
 // nb < 32: append the next word below the valid bits
 __device__ __forceinline__ void reader_refill(Reader &r, unsigned char *ring, const uint4 *src, int64_t bmax,
                                               uint64_t pol) {
-  r.ah |= r.q0 >> r.nb;
-  r.al |= __funnelshift_r(0u, r.q0, static_cast<uint32_t>(r.nb));  // q0 << (32 - nb); 0 when nb == 0
+  if ((r.wi & 3) == 0) reader_next_block(r, ring, src, bmax, pol);
+  const uint32_t w = bswap(*reinterpret_cast<const uint32_t *>(ring + (r.wi & (kSlots * 4 - 1)) * 4));
+  r.ah |= w >> r.nb;
+  r.al |= __funnelshift_r(0u, w, static_cast<uint32_t>(r.nb));  // w << (32 - nb); 0 when nb == 0
   r.nb += 32;
-  r.q0 = r.q1; r.q1 = r.q2; r.q2 = r.q3;
-  if (--r.qn == 0) reader_next_block(r, ring, src, bmax, pol);
+  ++r.wi;
 }
 
 // drop `n` (< 32) consumed bits
@@ -360,16 +357,17 @@ __device__ __forceinline__ void reader_init(Reader &r, unsigned char *ring, cons
 #pragma unroll
   for (int s = 0; s < kSlots - 1; ++s) cp_async16(ring + s * 16, src + min(b0 + s, bmax), pol);
   r.bi = b0 + kSlots - 1;
-  r.slot = 0;
-  reader_next_block(r, ring, src, bmax, pol);  // block b0 into q, request b0 + kSlots - 1
-  const int wofs = static_cast<int>((pos >> 2) & 3);
-  if (wofs & 2) { uint32_t t0 = r.q0, t1 = r.q1; r.q0 = r.q2; r.q1 = r.q3; r.q2 = t0; r.q3 = t1; }
-  if (wofs & 1) { uint32_t t0 = r.q0; r.q0 = r.q1; r.q1 = r.q2; r.q2 = r.q3; r.q3 = t0; }
-  r.qn = 4 - wofs;
+  r.wi = 0;
+  reader_next_block(r, ring, src, bmax, pol);  // block b0 landed; request block b0 + kSlots - 1
+  r.wi = static_cast<int>((pos >> 2) & 3);
   r.ah = 0;
   r.al = 0;
   r.nb = 0;
-  reader_refill(r, ring, src, bmax, pol);  // first word, then drop the bytes before the chunk start
+  // first word (block b0 is already entered), then drop the bytes before the chunk start
+  const uint32_t w = bswap(*reinterpret_cast<const uint32_t *>(ring + r.wi * 4));
+  r.ah = w;
+  r.nb = 32;
+  ++r.wi;
   reader_consume(r, static_cast<uint32_t>(pos & 3) * 8);
 }
 
@@ -433,8 +431,7 @@ __device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast,
     const int need = active ? static_cast<int>(min(cs, J.e1 - c * cs)) : 0;
 
     Reader rd;
-    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.q0 = rd.q1 = rd.q2 = rd.q3 = 0; rd.qn = 4; rd.bi = 0;
-    rd.slot = 0;
+    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.wi = 0; rd.bi = 0;
     if (active) {
       int64_t pos = static_cast<int64_t>(J.offs[c - J.chunk_base]) - J.offset_base;
       const int64_t nbyt = J.nbytes[c - J.chunk_base];
@@ -742,8 +739,7 @@ __device__ __forceinline__ void gemv_groups(const GemvJob &G, const uint2 *s_fas
     const uint8_t *smp = G.sm + cl * cs;
     const uint16_t *xp = G.x + static_cast<int64_t>(j) * cs;
     Reader rd;
-    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.q0 = rd.q1 = rd.q2 = rd.q3 = 0; rd.qn = 4; rd.bi = 0;
-    rd.slot = 0;
+    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.wi = 0; rd.bi = 0;
     if (active) {
       const int64_t c = G.c0 + cl;
       int64_t pos = static_cast<int64_t>(G.offs[c - G.chunk_base]) - G.offset_base;
