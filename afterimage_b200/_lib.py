@@ -20,6 +20,8 @@ _lib = None
 AIB_OK = 0
 AIB_EINVAL = 1
 AIB_ECUDA = 2
+AIB_EIO = 3
+AIB_ESHORT = 4
 AIB_MAX_BATCH = 16
 AIB_GEMV_SCRATCH_FLOATS = 1 << 20
 
@@ -80,6 +82,7 @@ SIGNATURES = [
     ("aib_chunk_nbytes", CI, [P, I64, I64, P, P, P]),
     ("aib_pack_chunks", CI, [P, I64, I64, P, P, P, P, P, I64]),
     ("aib_host_threads", CI, []),
+    ("aib_pread_batch", CI, [CI, P, P, P, P, I64, CI, P]),
     ("aib_tables_bytes", ctypes.c_size_t, []),
     ("aib_build_tables", CI, [P, P, CI, P, P]),
     ("aib_tables_flags", CI, [P, P, P]),
@@ -122,6 +125,8 @@ def check(rc: int, what: str = "") -> None:
     if rc == AIB_OK:
         return
     msg = load().aib_last_error().decode(errors="replace")
-    if rc == AIB_EINVAL:
+    if rc in (AIB_EINVAL, AIB_ESHORT):
         raise ValueError(f"{what}: {msg}" if what else msg)
+    if rc == AIB_EIO:
+        raise OSError(f"{what}: {msg}" if what else msg)
     raise AibError(f"{what}: {msg}" if what else msg)

@@ -25,7 +25,7 @@ LIBDIR = PKG / "lib"
 LIB = LIBDIR / "libafterimage_b200.so"
 
 CU_SOURCES = ["decode.cu"]
-CPP_SOURCES = ["encode.cpp"]
+CPP_SOURCES = ["encode.cpp", "io.cpp"]
 HEADERS = ["aib_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

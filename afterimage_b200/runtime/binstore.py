@@ -95,28 +95,14 @@ class PinnedBuffer:
         return self._t
 
 
-_POOLS: dict = {}
-_POOLS_LOCK = __import__("threading").Lock()
-
-
-def _pool(threads: int):
-    """Process-wide reader pool (threads release the GIL inside preadv)."""
-    import concurrent.futures
-    with _POOLS_LOCK:
-        pool = _POOLS.get(threads)
-        if pool is None:
-            pool = concurrent.futures.ThreadPoolExecutor(max_workers=threads, thread_name_prefix="aib-read")
-            _POOLS[threads] = pool
-        return pool
-
-
 class BinaryWeightReader:
     """One open file handle for the store's lifetime.
 
-    `threads` > 1 splits the pinned reads of `read_many` into pieces of at
-    least `piece_bytes` read concurrently with positional reads (one
-    thread's page-cache copy rate is a few GB/s; a PCIe 5 link takes
-    ~55 GB/s)."""
+    `threads` > 1 reads the pinned extents of `read_many` in pieces of
+    `piece_bytes` with the library's native thread pool (aib_pread_batch),
+    outside the interpreter lock: one thread's page-cache copy rate is a
+    few GB/s, and Python reader threads stall on the lock held by the
+    forward pass."""
 
     def __init__(self, path, direct: bool = False, threads: int = 1, piece_bytes: int = 8 << 20):
         self.path = pathlib.Path(path)
@@ -154,40 +140,43 @@ class BinaryWeightReader:
             got += k
         return got
 
-    def _readinto_parallel(self, start: int, view: memoryview, direct: bool) -> int:
-        """Fills `view` from [start, start + len(view)) in pieces on the
-        reader pool; returns the bytes read (short only at end of file)."""
-        n = len(view)
-        step = self.piece_bytes
-        fd = self._direct_fd if direct else self._fd
-        jobs = [(o, min(step, n - o)) for o in range(0, n, step)]
-        futs = [_pool(self.threads).submit(self._pread_full, fd, start + o, view[o:o + m]) for o, m in jobs]
-        got = [f.result() for f in futs]
-        total = 0
-        for (o, m), g in zip(jobs, got):
-            total += g
-            if g < m:
-                return total
-        return total
+    def _native_reads(self, fd: int, spans: list[tuple[int, int, int, int]]) -> None:
+        """spans: (file offset, bytes to read, bytes needed, destination
+        address). Cut into pieces of piece_bytes and read by the library's
+        thread pool in one call (outside the interpreter lock)."""
+        import ctypes
+        from .. import _lib
+        offs, sizes, need, dests = [], [], [], []
+        for start, size, needed, addr in spans:
+            for o in range(0, size, self.piece_bytes):
+                m = min(self.piece_bytes, size - o)
+                offs.append(start + o)
+                sizes.append(m)
+                need.append(max(0, min(m, needed - o)))
+                dests.append(addr + o)
+        n = len(offs)
+        if n == 0:
+            return
+        A = ctypes.c_int64 * n
+        D = ctypes.c_void_p * n
+        got = ctypes.c_int64(0)
+        L = _lib.load()
+        _lib.check(L.aib_pread_batch(fd, A(*offs), A(*sizes), A(*need), D(*dests), n, self.threads,
+                                     ctypes.byref(got)), "read_many")
 
     def _readinto(self, start: int, view: memoryview) -> int:
         """Fill `view` with file bytes [start, start + len(view)). O_DIRECT
         when enabled and the destination/offset/length are sector aligned
         (retrying buffered on EINVAL); buffered otherwise."""
         n = len(view)
-        parallel = self.threads > 1 and n > self.piece_bytes
         if self._direct_fd is not None and n and start % _DIRECT_ALIGN == 0:
             addr = np.frombuffer(view, dtype=np.uint8).ctypes.data
             if addr % _DIRECT_ALIGN == 0:
                 try:
-                    if parallel:
-                        return self._readinto_parallel(start, view, True)
                     return self._pread_full(self._direct_fd, start, view)
                 except OSError:
                     os.close(self._direct_fd)
                     self._direct_fd = None
-        if parallel:
-            return self._readinto_parallel(start, view, False)
         self._fh.seek(start)
         return self._fh.readinto(view)
 
@@ -236,13 +225,34 @@ class BinaryWeightReader:
 
         out: list = [None] * len(refs)
         bytes_read = 0
+        if buf is not None and self.threads > 1:
+            # every extent of the call in one native batch of parallel positional reads
+            base = arena.ctypes.data
+            if self.direct:
+                spans = []
+                for e in extents:
+                    lead = e["start"] % _DIRECT_ALIGN
+                    span = (lead + e["end"] - e["start"] + _DIRECT_ALIGN - 1) // _DIRECT_ALIGN * _DIRECT_ALIGN
+                    spans.append((e["start"] - lead, span, lead + e["end"] - e["start"], base + e["slot"] - lead))
+                try:
+                    self._native_reads(self._direct_fd, spans)
+                except OSError:
+                    os.close(self._direct_fd)
+                    self._direct_fd = None
+            if not self.direct:
+                self._native_reads(self._fd, [(e["start"], e["end"] - e["start"], e["end"] - e["start"],
+                                              base + e["slot"]) for e in extents])
+            for e in extents:
+                e["done"] = True
         for e in extents:
             start, nbytes = e["start"], e["end"] - e["start"]
             if buf is not None:
                 lead = start % _DIRECT_ALIGN
                 a0 = e["slot"] - lead
                 span = (lead + nbytes + _DIRECT_ALIGN - 1) // _DIRECT_ALIGN * _DIRECT_ALIGN
-                if self.direct:
+                if e.get("done"):
+                    got = nbytes
+                elif self.direct:
                     got = self._readinto(start - lead, memoryview(arena[a0:a0 + span]))
                     got = min(max(0, got - lead), nbytes)
                 else:

@@ -40,7 +40,7 @@ import torch
 from . import _device
 from . import gpu_decode_v2 as _gd
 from .binstore import BinaryWeightReader, BinaryWeightWriter, PinnedBuffer, blobref_to_dict
-from .compressed_store import CompressedLayer, compress_layer, decompress_layer_gpu
+from .compressed_store import decompress_rows_gpu, CompressedLayer, compress_layer, decompress_layer_gpu
 from .huffman_chunked import ChunkedEncoded
 from .layer_decode import LayerDecoder, ResidentLayer, upload_layer
 from .verify import sample_categorical, speculative_sample_step, temperature_probs
@@ -71,6 +71,8 @@ class EngineConfig:
     max_context: int | None = None
     vram_cap_gb: float | None = None
     spec_k: int = 8
+    lm_head_slice_rows: int = 0             # reference config: rows of lm_head per block, 0 = whole
+    max_inflight_layers: int = 2            # streamed layers whose device buffers may be alive at once
 
     def __post_init__(self):
         if self.chunk_size < 1:
@@ -83,6 +85,10 @@ class EngineConfig:
             raise ValueError("io_prefetch_depth must be >= 0")
         if self.io_threads < 1:
             raise ValueError("io_threads must be >= 1")
+        if self.lm_head_slice_rows < 0:
+            raise ValueError("lm_head_slice_rows must be >= 0")
+        if self.max_inflight_layers < 1:
+            raise ValueError("max_inflight_layers must be >= 1")
         if self.ram_tier_format not in ("decoded", "compressed"):
             raise ValueError("ram_tier_format must be 'decoded' or 'compressed'")
         if self.vram_tier_format not in ("decoded", "compressed"):
@@ -287,6 +293,34 @@ def compress_model_to_disk(model_id: str, out_dir, config: EngineConfig | None =
 # online engine
 # ---------------------------------------------------------------------------
 
+def layer_working_set(manifest: dict) -> int:
+    """Device bytes one streamed decoder layer holds while it runs: its
+    compressed upload plus its decoded weights (upper bound: every tensor of
+    the layer streamed; a layer is decoded by one launch)."""
+    per: dict[int, int] = {}
+    for key, meta in manifest["tensors"].items():
+        if key.startswith("model.layers.") and not meta.get("row_gather"):
+            i = int(key.split(".")[2])
+            per[i] = per.get(i, 0) + int(meta["orig_bytes"]) + int(meta.get("comp_bytes", 0))
+    return max(per.values(), default=0)
+
+
+def engine_headroom_bytes(manifest: dict, cfg: EngineConfig, stream_only: dict | None = None,
+                          activation_slack_bytes: int | None = None) -> int:
+    """VRAM the streaming engine keeps free of resident tensors: the larger
+    of the biggest tensor it materialises and `max_inflight_layers` streamed
+    layers, plus decode scratch and activations."""
+    from .vram_planner import DEFAULT_ACTIVATION_SLACK_BYTES, decode_scratch_bytes
+    stream_only = stream_only or {}
+    largest = 0
+    for key, meta in manifest["tensors"].items():
+        if not meta.get("row_gather"):
+            largest = max(largest, int(stream_only.get(key, meta["orig_bytes"])))
+    slack = DEFAULT_ACTIVATION_SLACK_BYTES if activation_slack_bytes is None else activation_slack_bytes
+    return (max(largest, cfg.max_inflight_layers * layer_working_set(manifest))
+            + decode_scratch_bytes(cfg.decode_slice_elems) + slack)
+
+
 def _split_key(root: torch.nn.Module, key: str):
     mod_path, _, name = key.rpartition(".")
     return (root.get_submodule(mod_path) if mod_path else root), name
@@ -406,6 +440,7 @@ class StreamingLosslessModel:
                               for _ in self._slots]
         self._pool = concurrent.futures.ThreadPoolExecutor(max_workers=max(1, depth), thread_name_prefix="aib-io")
         self._futures: dict[int, concurrent.futures.Future] = {}
+        self._inflight: list = []   # (layer, compute-stream event after its forward), oldest first
 
         self._materialize_resident()
         self._install_hooks()
@@ -438,25 +473,55 @@ class StreamingLosslessModel:
                 keys.append(key)
         return keys
 
+    def _chunked_head_rows(self) -> int:
+        """Rows of lm_head per block, or 0 when chunking is off or does not
+        apply: a tied head has no tensor of its own and a raw-stored head no
+        chunk ranges (reference streaming_engine.py:877-892)."""
+        if self.config.lm_head_slice_rows <= 0:
+            return 0
+        meta = self.manifest["tensors"].get(self.CHUNKED_HEAD_KEY)
+        if not meta or not meta.get("compressed") or len(meta["shape"]) != 2:
+            return 0
+        return self.config.lm_head_slice_rows
+
+    def _stream_only_overrides(self) -> dict:
+        """{key: bytes live at once} for tensors computed in blocks and never
+        held whole (reference :894-902)."""
+        step = self._chunked_head_rows()
+        if not step:
+            return {}
+        rows, cols = self.manifest["tensors"][self.CHUNKED_HEAD_KEY]["shape"]
+        return {self.CHUNKED_HEAD_KEY: min(step, rows) * cols * 2}
+
     def _compute_tier_assignment(self) -> dict[str, str]:
         """key -> "vram" | "ram" | "disk" | "row_gather" (reference
         streaming_engine.py:904-1043): without a budget every decoder-layer
         tensor streams and everything else is resident; with one, the
-        planner ranks all tensors."""
+        planner ranks all tensors. A chunked head always streams.
+
+        The headroom given to the planner is this engine's working set: the
+        largest tensor it materialises, or `max_inflight_layers` streamed
+        layers (each a compressed upload plus its decoded weights, since a
+        layer is decoded by one launch), whichever is larger, plus decode
+        scratch and activations -- so the budget bounds the measured peak."""
         cfg = self.config
         tiers = {k: "row_gather" for k, m in self.manifest["tensors"].items() if m.get("row_gather")}
+        chunked = self.CHUNKED_HEAD_KEY if self._chunked_head_rows() else None
+        if chunked:
+            tiers[chunked] = "disk"
         if not cfg.uses_tiered_residency:
             for key in self.manifest["tensors"]:
                 tiers.setdefault(key, "disk" if key.startswith("model.layers.") else "vram")
             return tiers
         from .vram_planner import DEFAULT_ACTIVATION_SLACK_BYTES, kv_cache_bytes_per_token, plan_from_manifest
-        kw = {}
+        slack = DEFAULT_ACTIVATION_SLACK_BYTES
         if cfg.max_context is not None:
-            kw["activation_slack_bytes"] = (DEFAULT_ACTIVATION_SLACK_BYTES
-                                            + kv_cache_bytes_per_token(self.hf_cfg) * cfg.max_context)
+            slack += kv_cache_bytes_per_token(self.hf_cfg) * cfg.max_context
+        stream_only = self._stream_only_overrides()
+        headroom = engine_headroom_bytes(self.manifest, cfg, stream_only, slack)
         plan = plan_from_manifest(self.manifest, vram_budget_gb=cfg.vram_budget_gb,
-                                  ram_budget_gb=cfg.ram_budget_gb or 0.0,
-                                  decode_slice_elems=cfg.decode_slice_elems, **kw)
+                                  ram_budget_gb=cfg.ram_budget_gb or 0.0, stream_only=stream_only,
+                                  vram_headroom_bytes=headroom)
         if not plan.feasible:
             raise RuntimeError("VRAM budget is infeasible: " + plan.reason)
         self.plan = plan
@@ -630,7 +695,16 @@ class StreamingLosslessModel:
         for k, o in zip(keys, outs):
             _set_param(module_root, k, o)
 
+    def _bound_inflight(self, keep: int) -> None:
+        """Waits until at most `keep` earlier streamed layers can still hold
+        device buffers (the host otherwise runs layers ahead of the GPU and
+        their uploads and decoded weights pile up past the VRAM budget)."""
+        while len(self._inflight) > keep:
+            _, ev = self._inflight.pop(0)
+            ev.synchronize()
+
     def _load_layer(self, idx: int) -> None:
+        self._bound_inflight(self.config.max_inflight_layers - 1)
         compute = torch.cuda.current_stream(self.device)
         arrays, slot = self._fetch_layer(idx)
         for ahead in range(1, self.config.io_prefetch_depth + 1):
@@ -669,6 +743,9 @@ class StreamingLosslessModel:
         self.stats.layer_loads += 1
 
     def _free_layer(self, idx: int) -> None:
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self._inflight.append((idx, ev))
         for k in self._layer_keys[idx]:
             if self.tier_of(k) == "vram" and k not in self._vram_compressed:
                 continue
@@ -697,13 +774,15 @@ class StreamingLosslessModel:
         """Non-layer tensors that the plan leaves on disk (e.g. lm_head at a
         small budget) are decoded just before their module runs."""
         groups: dict[str, list[str]] = {}
+        chunked = self.CHUNKED_HEAD_KEY if self._chunked_head_rows() else None
         for key, tier in self._tier.items():
-            if tier == "disk" and not key.startswith("model.layers."):
+            if tier == "disk" and not key.startswith("model.layers.") and key != chunked:
                 groups.setdefault(key.rpartition(".")[0], []).append(key)
         for mod_name, keys in groups.items():
             mod = self.model.get_submodule(mod_name)
 
             def pre(module, args, keys=keys):
+                self._bound_inflight(0)
                 arrays = self._read_arrays(keys, self._reader, pinned=False)
                 for k in keys:
                     _set_param(self.model, k, self._decode_whole(k, arrays[k]))
@@ -714,6 +793,34 @@ class StreamingLosslessModel:
                 return output
             mod.register_forward_pre_hook(pre)
             mod.register_forward_hook(post)
+        if chunked:
+            self._install_chunked_lm_head()
+
+    def _install_chunked_lm_head(self) -> None:
+        """Logits in row blocks instead of a materialised lm_head (reference
+        streaming_engine.py:2271-2334): logits[..., a:b] = x @ W[a:b].T, each
+        block decoded from its chunk range by decompress_rows_gpu, so only
+        one block's weights are live. The compressed bytes are read once per
+        forward; the result is the same matmul in pieces."""
+        step = self._chunked_head_rows()
+        key = self.CHUNKED_HEAD_KEY
+        meta = self.manifest["tensors"][key]
+        rows = int(meta["shape"][0])
+
+        def forward(x: torch.Tensor) -> torch.Tensor:
+            self._bound_inflight(0)
+            arrays = self._read_arrays([key], self._reader, pinned=False)[key]
+            layer = _encoded_from_arrays(meta, arrays)
+            parts = []
+            for r0 in range(0, rows, step):
+                t0 = time.perf_counter()
+                W = decompress_rows_gpu(layer, r0, min(rows, r0 + step), device=self.device)
+                self.stats.decode_seconds += time.perf_counter() - t0
+                parts.append(torch.nn.functional.linear(x, W))
+                del W
+            return torch.cat(parts, dim=-1)
+
+        self.model.lm_head.forward = forward
 
     # -- inference --------------------------------------------------------------
     @torch.no_grad()

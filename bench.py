@@ -235,8 +235,11 @@ def run_tokens(args, dev) -> dict:
                "store_gb": round(m["total_comp_bytes"] / 1e9, 2), "ratio": round(m["ratio"], 4),
                "store_build_s": round(build_s, 1), "prompt_tokens": 64, "new_tokens": args.new_tokens}
         ref_tokens = None
-        for name, ecfg in (("streamed_4GB", EngineConfig(vram_budget_gb=4.0, io_prefetch_depth=4)),
+        for name, ecfg in (("streamed_4GB", EngineConfig(vram_budget_gb=4.0, io_prefetch_depth=4,
+                                                          lm_head_slice_rows=16384)),
                            ("resident_compressed", EngineConfig(vram_budget_gb=100.0, vram_tier_format="compressed"))):
+            torch.cuda.empty_cache()
+            torch.cuda.reset_peak_memory_stats(dev)
             with StreamingLosslessModel("synthetic/qwen3-14b-shape", root / "qwen3-14b", device=str(dev),
                                         config=ecfg, hf_config=cfg) as eng:
                 eng.generate_greedy(prompt, 1)  # warm: kernels, tables, allocator
@@ -251,6 +254,9 @@ def run_tokens(args, dev) -> dict:
                              "bytes_read_gb": round(st.bytes_read / 1e9, 2), "h2d_gb": round(st.h2d_bytes / 1e9, 2),
                              "decode_launches": st.decode_launches, "prefetch_hits": st.prefetch_hits,
                              "prefetch_misses": st.prefetch_misses,
+                             "io_s": round(st.io_seconds, 3), "h2d_enqueue_s": round(st.h2d_seconds, 3),
+                             "decode_enqueue_s": round(st.decode_seconds, 3),
+                             "vram_budget_gb": ecfg.vram_budget_gb,
                              "peak_vram_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 2)}
                 if ref_tokens is None:
                     ref_tokens = seq

@@ -29,6 +29,8 @@ extern "C" {
 #define AIB_OK 0
 #define AIB_EINVAL 1 /* bad argument: caught on the host before any launch */
 #define AIB_ECUDA 2  /* a CUDA runtime call failed */
+#define AIB_EIO 3    /* a host read failed */
+#define AIB_ESHORT 4 /* a host read ended before the requested bytes (end of file) */
 
 /* Bits the decode kernels OR into the optional device status word. */
 #define AIB_STATUS_BAD_CHUNK_RANGE 1 /* a chunk's [offset, offset + nbytes) lies outside packed */
@@ -69,6 +71,21 @@ int aib_pack_chunks(const uint8_t *symbols, int64_t n, int64_t chunk_size,
                     int64_t out_capacity);
 /* Host threads the encoder uses (OpenMP). */
 int aib_host_threads(void);
+
+/* ------------------------------------------------------------------------
+ * Store reads -- the extents of BinaryWeightReader.read_many
+ * (afterimage/runtime/binstore.py:109-192)
+ * ------------------------------------------------------------------------ */
+/* n positional reads of file descriptor fd: piece i fills dests[i] with
+ * sizes[i] bytes from offsets[i]. `threads` host threads read pieces
+ * concurrently; *bytes_read receives the bytes read. If min_sizes is not
+ * NULL, a piece that reaches end of file after min_sizes[i] bytes is
+ * complete (O_DIRECT reads round their size up past the end of the file).
+ * Returns AIB_ESHORT if the file ends early, AIB_EIO for a read error
+ * (the message names the piece). Works with O_DIRECT descriptors when
+ * offsets, sizes and dests meet its alignment. */
+int aib_pread_batch(int fd, const int64_t *offsets, const int64_t *sizes, const int64_t *min_sizes,
+                    void *const *dests, int64_t n, int threads, int64_t *bytes_read);
 
 /* ------------------------------------------------------------------------
  * Decode tables -- replaces prepare_decode_tables

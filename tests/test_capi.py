@@ -138,3 +138,40 @@ def test_encoder_entry_points_via_c_abi():
     assert L.aib_histogram(e.ctypes.data, 8, counts.ctypes.data) == 0
     assert counts.sum() == 8
     assert L.aib_build_code(counts.ctypes.data, 0, None, None, None) == _lib.AIB_EINVAL
+
+
+def test_pread_batch_reads_pieces_in_parallel(tmp_path):
+    import os
+    L = _lib.load()
+    data = np.random.default_rng(3).integers(0, 256, 1 << 20, dtype=np.uint8)
+    path = tmp_path / "f.bin"
+    data.tofile(path)
+    fd = os.open(path, os.O_RDONLY)
+    try:
+        pieces = [(0, 4096), (4096, 70000), (500000, 3), (1048000, 576), (123, 0)]
+        dst = np.zeros(sum(n for _, n in pieces), dtype=np.uint8)
+        offs, sizes, dests, pos = [], [], [], 0
+        for o, n in pieces:
+            offs.append(o), sizes.append(n), dests.append(dst.ctypes.data + pos)
+            pos += n
+        A = ctypes.c_int64 * len(pieces)
+        D = ctypes.c_void_p * len(pieces)
+        got = ctypes.c_int64(-1)
+        assert L.aib_pread_batch(fd, A(*offs), A(*sizes), None, D(*dests), len(pieces), 4,
+                                 ctypes.byref(got)) == _lib.AIB_OK
+        assert got.value == dst.size
+        want = np.concatenate([data[o:o + n] for o, n in pieces])
+        assert np.array_equal(dst, want)
+        # past the end of the file: short unless min_sizes allows it
+        tail = np.zeros(8192, dtype=np.uint8)
+        one = (ctypes.c_int64 * 1)
+        args = (fd, one((1 << 20) - 100), one(8192))
+        assert L.aib_pread_batch(*args, None, (ctypes.c_void_p * 1)(tail.ctypes.data), 1, 2,
+                                 ctypes.byref(got)) == _lib.AIB_ESHORT
+        assert b"short read" in L.aib_last_error()
+        assert L.aib_pread_batch(*args, one(100), (ctypes.c_void_p * 1)(tail.ctypes.data), 1, 2,
+                                 ctypes.byref(got)) == _lib.AIB_OK
+        assert np.array_equal(tail[:100], data[-100:])
+    finally:
+        os.close(fd)
+    assert L.aib_pread_batch(-1, None, None, None, None, 0, 1, None) == _lib.AIB_EINVAL

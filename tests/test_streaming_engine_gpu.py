@@ -72,12 +72,12 @@ def test_logits_bit_exact_vs_plain_forward(untied, depth):
 def test_tiered_residency_is_bit_exact(untied, tiers):
     """Budgets are set as a fraction of the model's bytes above the
     planner's fixed headroom, so the cases mix VRAM, RAM and disk tiers."""
-    from afterimage_b200.runtime.vram_planner import DEFAULT_ACTIVATION_SLACK_BYTES, decode_scratch_bytes
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, engine_headroom_bytes
     cfg, model, snap, store, manifest = untied
     t = {k: v for k, v in manifest["tensors"].items() if not v.get("row_gather")}
     total = sum(v["orig_bytes"] for v in t.values())
     slice_elems = 1 << 16
-    head = max(v["orig_bytes"] for v in t.values()) + decode_scratch_bytes(slice_elems) + DEFAULT_ACTIVATION_SLACK_BYTES
+    head = engine_headroom_bytes(manifest, EngineConfig(decode_slice_elems=slice_elems))
     kw = dict(tiers)
     kw["vram_budget_gb"] = (head + kw.pop("vram") * total) / 1e9
     if "ram" in kw:
@@ -92,6 +92,48 @@ def test_tiered_residency_is_bit_exact(untied, tiers):
     assert torch.equal(got, ref) and torch.equal(got2, ref), kinds
     if tiers.get("vram", 0) < 1:
         assert "disk" in kinds or "ram" in kinds, kinds
+
+
+@pytest.mark.parametrize("rows", [500, 1536, 4096])
+def test_chunked_lm_head_streams_in_row_blocks(untied, rows):
+    """lm_head_slice_rows: the head stays on the meta device and logits are
+    computed a row block at a time (reference streaming_engine.py:2271-2334);
+    greedy tokens equal, logits within BF16 GEMM reassociation."""
+    cfg, model, snap, store, _ = untied
+    ids = torch.randint(0, cfg.vocab_size, (1, 7), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits
+    with _engine(snap, store, lm_head_slice_rows=rows, vram_budget_gb=1.0) as eng:
+        assert eng.tier_of("lm_head.weight") == "disk"
+        assert eng.model.lm_head.weight.device.type == "meta"
+        got = eng.forward_logits(ids)
+        assert eng.model.lm_head.weight.device.type == "meta"
+    assert torch.allclose(got.float(), ref.float(), atol=2e-2, rtol=0)
+    assert torch.equal(got.argmax(-1), ref.argmax(-1))
+
+
+@pytest.mark.parametrize("inflight", [1, 2, 3])
+def test_streamed_peak_vram_stays_within_budget(untied, inflight):
+    """With a budget the planner reserves the engine's working set (the
+    in-flight streamed layers), and the engine never lets more layers than
+    that hold device buffers: the measured peak stays under the budget."""
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, engine_headroom_bytes
+    cfg, model, snap, store, manifest = untied
+    budget = (engine_headroom_bytes(manifest, EngineConfig(max_inflight_layers=inflight, decode_slice_elems=1 << 16))
+              + 2_000_000) / 1e9
+    ids = torch.randint(0, cfg.vocab_size, (1, 9), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits
+    model_bytes = torch.cuda.memory_allocated()
+    torch.cuda.reset_peak_memory_stats()
+    with _engine(snap, store, vram_budget_gb=budget, max_inflight_layers=inflight, decode_slice_elems=1 << 16,
+                 io_prefetch_depth=2) as eng:
+        got = eng.forward_logits(ids)
+        seq = eng.generate_greedy(ids, 3)
+        peak = torch.cuda.max_memory_allocated() - model_bytes
+    assert torch.equal(got, ref)
+    assert seq.shape == (1, 12)
+    assert peak <= budget * 1e9, (peak, budget)
 
 
 def test_greedy_matches_reference_argmax_loop_and_kv_cache(untied):
