@@ -1181,11 +1181,36 @@ AIB_API int aib_decode_gemv_bf16_batch(const aib_gemv_desc *descs, int count, in
   return gemv_launch(descs, count, d_status, stream);
 }
 
-// Library-owned scratch for aib_decode_gemv_bf16_batch_noalloc: callers that
-// only hold device pointers handed to them (no allocator of their own) get
-// the per-chunk partial sums placed here. One array per device context,
-// shared by all such calls, so they must be stream-ordered.
+// Library-owned scratch for aib_decode_gemv_bf16_batch_noalloc. Some callers
+// cannot allocate device memory themselves: a binding from another host
+// language that only receives device pointers from the framework owning the
+// memory, or code running under a framework whose allocator must see every
+// byte (a VRAM budget that a side cudaMalloc would silently break). They get
+// the per-chunk partial sums placed here instead: AIB_GEMV_SCRATCH_FLOATS
+// floats (4 MiB), held by every GPU that loads the library until exit. In
+// host code the array's name is only a stand-in for the device copy; its
+// device address is looked up once per device (below) and passed on.
 static __device__ __align__(256) float g_gemv_scratch[AIB_GEMV_SCRATCH_FLOATS];
+
+static float *g_scratch_addr[64];
+static std::mutex g_scratch_mu;
+
+// Device address of g_gemv_scratch on the current device, looked up with
+// cudaGetSymbolAddress on the first call for that device.
+static int scratch_address(float **out) {
+  int dev = 0;
+  AIB_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return aib_set_error("device index out of range"), AIB_EINVAL;
+  std::lock_guard<std::mutex> lk(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void *p = nullptr;
+    AIB_CUDA(cudaGetSymbolAddress(&p, g_gemv_scratch));
+    if (!p) return aib_set_error("gemv: no device address for the library scratch"), AIB_ECUDA;
+    g_scratch_addr[dev] = static_cast<float *>(p);
+  }
+  *out = g_scratch_addr[dev];
+  return AIB_OK;
+}
 
 AIB_API int aib_decode_gemv_bf16_batch_noalloc(const aib_gemv_desc *descs, int count, int32_t *d_status,
                                                void *stream) {
@@ -1209,8 +1234,11 @@ AIB_API int aib_decode_gemv_bf16_batch_noalloc(const aib_gemv_desc *descs, int c
     return aib_set_errorf("gemv: the batch needs %lld scratch floats, the library holds %d", (long long)total,
                           AIB_GEMV_SCRATCH_FLOATS),
            AIB_EINVAL;
+  // Nothing in the scratch has to start at zero: the decode kernel writes
+  // every partial sum of the batch before the row kernel reads it.
   float *base = nullptr;
-  AIB_CUDA(cudaGetSymbolAddress(reinterpret_cast<void **>(&base), g_gemv_scratch));
+  const int rc = scratch_address(&base);
+  if (rc != AIB_OK) return rc;
   aib_gemv_desc local[AIB_MAX_BATCH];
   int64_t off = 0;
   for (int i = 0; i < count; ++i) {

@@ -176,17 +176,24 @@ typedef struct aib_gemv_desc {
  * (deterministic). Work is enqueued on `stream`; no synchronisation. */
 int aib_decode_gemv_bf16_batch(const aib_gemv_desc *descs, int count, int32_t *d_status, void *stream);
 
-/* The same fused decode -> GEMV with no caller scratch: the per-chunk
- * partial sums go to a fixed device array inside the library
- * (AIB_GEMV_SCRATCH_FLOATS floats for the whole batch; descs[i].partial is
- * ignored). For callers that receive the tensor, x and y as device pointers
- * from someone else and have no device allocator of their own -- a binding
- * from a host language over this C ABI that is handed buffers by another
- * framework, for example. The array is shared by every call of the process
- * on the device, so calls must be ordered on one stream (two such calls
- * running concurrently on different streams would overwrite each other's
- * partial sums). A batch that needs more scratch returns AIB_EINVAL before
- * touching the device. */
+/* The same fused decode -> GEMV for callers that cannot allocate device
+ * memory: it has no counterpart in the reference. Such callers hold only
+ * the device pointers someone else gave them -- a binding from another host
+ * language that is handed buffers by the framework owning the memory, or a
+ * caller under a framework whose allocator must account for every byte, so
+ * a side cudaMalloc would break its budget. The caller passes the stream
+ * descriptors, x and y as for aib_decode_gemv_bf16_batch; descs[i].partial
+ * is ignored, and the per-chunk partial sums go to a fixed array inside the
+ * library instead (AIB_GEMV_SCRATCH_FLOATS floats, 4 MiB, held by every
+ * GPU that loads the library until the process exits). A batch needing
+ * more than that returns AIB_EINVAL before touching the device; nothing is
+ * allocated. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress) and caches it: make that first call before
+ * any stream capture. The array is shared by every call of the process on
+ * that device and keeps the last call's contents (nothing in it needs to
+ * start at zero: each call writes every partial it reads); two calls that
+ * overlap on the GPU -- different streams, no ordering between them --
+ * race on it and corrupt each other's results. */
 #define AIB_GEMV_SCRATCH_FLOATS (1 << 20)
 int aib_decode_gemv_bf16_batch_noalloc(const aib_gemv_desc *descs, int count, int32_t *d_status, void *stream);
 
