@@ -243,6 +243,8 @@ class _StepState:
         self.arange = torch.arange(max_len, device=dev).view(1, max_len)
         self.mask = torch.zeros(1, max_len, dtype=torch.bool, device=dev)  # [query, key]
         self.graph = None
+        self.prefill: dict = {}   # prompt length -> (graph, static prompt buffer)
+        self.pool = torch.cuda.graph_pool_handle()
 
 
 class TPDecoder:
@@ -403,10 +405,12 @@ class TPDecoder:
 
     @torch.no_grad()
     def generate_greedy_graphed(self, input_ids: torch.Tensor, max_new_tokens: int) -> torch.Tensor:
-        """Greedy decoding with the single-token step captured once as a CUDA
-        graph (decode launches, projections, all-reduces, argmax and the
-        position update) and replayed per token; the prompt runs eagerly.
-        The embedding must be on the device."""
+        """Greedy decoding from CUDA graphs: the prompt pass is captured once
+        per prompt length (static shapes: positions 0..P-1, causal mask) and
+        the single-token step once (decode launches, projections,
+        all-reduces, argmax and the position update); both are replayed.
+        Each graph is captured after one eager run of the same work (cuBLAS,
+        NCCL and allocator state). The embedding must be on the device."""
         if callable(self.w.get("model.embed_tokens.weight")) or getattr(self, "mode", None) == "streamed":
             raise ValueError("graphed generation needs device-resident weights and embedding "
                              "(resident='decoded' or 'compressed')")
@@ -419,17 +423,27 @@ class TPDecoder:
             self.release_graphs()
             st = _StepState(self, max(128, P + max_new_tokens))
             self._graph_state = st
-        st.cache.length = 0
-        logits = self.forward(ids, st.cache)
-        first = logits[-1:].argmax(-1).reshape(1)
+        pre = st.prefill.get(P)
+        if pre is None:
+            buf = ids.reshape(-1).clone()
+            self._prefill_into(st, buf)  # eager run of the same work
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=st.pool):
+                self._prefill_into(st, buf)
+            pre = (g, buf)
+            st.prefill[P] = pre
+        g, buf = pre
+        buf.copy_(ids.reshape(-1))
+        g.replay()
+        first = st.ids.clone()
         if max_new_tokens == 1:
             return torch.cat([ids, first.reshape(1, 1)], 1)
-        st.ids.copy_(first)
         st.pos.fill_(P)
         st.step.zero_()
         todo = max_new_tokens - 1
         if st.graph is None:
-            # one real step eagerly on a side stream (allocator pools, library and NCCL state), then capture
+            # one real step eagerly on a side stream, then capture
             cur = torch.cuda.current_stream(self.device)
             side = torch.cuda.Stream(self.device)
             side.wait_stream(cur)
@@ -439,12 +453,19 @@ class TPDecoder:
             torch.cuda.synchronize(self.device)
             todo -= 1
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
+            with torch.cuda.graph(g, pool=st.pool):
                 self._static_step(st)
             st.graph = g
         for _ in range(todo):
             st.graph.replay()
         return torch.cat([ids, first.reshape(1, 1), st.tokens[:max_new_tokens - 1].reshape(1, -1)], 1)
+
+    def _prefill_into(self, st: "_StepState", prompt: torch.Tensor) -> None:
+        """The prompt pass from an empty cache, leaving its greedy token in
+        st.ids (static shapes for a fixed prompt length)."""
+        st.cache.length = 0
+        logits = self.forward(prompt, st.cache)
+        st.ids.copy_(logits[-1:].argmax(-1).reshape(1))
 
     @torch.no_grad()
     def replay_steps(self, n: int) -> int:

@@ -439,8 +439,8 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
                                    "s_per_token": round(gms / 1e3 / args.new_tokens, 4),
                                    "tokens_equal_eager": bool(torch.equal(gseq.cpu(), seqs[name])),
                                    "step_ms": round(sms, 3), "step_tokens_per_s": round(1e3 / sms, 2),
-                                   "note": "tokens_per_s includes the eager 64-token prefill; step_ms is one "
-                                           "replay of the captured single-token step"}
+                                   "note": "tokens_per_s includes the 64-token prompt pass (a captured graph "
+                                           "too); step_ms is one replay of the captured single-token step"}
                 dec.release_graphs()
             if resident == "streamed":
                 hb = dec.h2d_bytes_per_forward()

@@ -80,16 +80,17 @@ def test_tp_graphed_generation(stores, resident, kw):
     cfg, model, store, tp_store = stores
     dec = load_tp_decoder(tp_store, cfg, 1, 0, None, "cuda", resident=resident, **kw)
     model = model.to("cuda")
-    for seed in (3, 4):
-        ids = torch.randint(0, cfg.vocab_size, (1, 9), device="cuda",
+    for seed, P in ((3, 9), (4, 9), (5, 12), (6, 9)):
+        ids = torch.randint(0, cfg.vocab_size, (1, P), device="cuda",
                             generator=torch.Generator(device="cuda").manual_seed(seed))
         seq = dec.generate_greedy_graphed(ids, 6)
         eager = dec.generate_greedy(ids, 6)
         ref_seq, margins = _ref_greedy(model, ids, 6)
-        _check_greedy(seq, ref_seq, margins, 9)
-        _check_greedy(seq, eager, margins, 9)
-        assert seq.shape == (1, 15)
-    assert dec._graph_state is not None and dec._graph_state.graph is not None
+        _check_greedy(seq, ref_seq, margins, P)
+        _check_greedy(seq, eager, margins, P)
+        assert seq.shape == (1, P + 6)
+    st = dec._graph_state
+    assert st is not None and st.graph is not None and sorted(st.prefill) == [9, 12]
     if resident != "decoded":
         _lib_status_clear()
     dec.close()
