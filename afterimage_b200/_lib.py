@@ -93,6 +93,10 @@ SIGNATURES = [
     ("aib_decode_gemv_bf16_batch", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
     ("aib_decode_gemv_bf16_batch_noalloc", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
     ("aib_recombine", CI, [P, P, I64, P, P]),
+    ("aib_add_rmsnorm_bf16", CI, [P, P, P, P, I64, I64, ctypes.c_float, P]),
+    ("aib_qk_rope_cache_bf16", CI, [P, CI, CI, CI, CI, P, P, ctypes.c_float, P, P, P, P, P, I64, P]),
+    ("aib_decode_attention_bf16", CI, [P, P, P, CI, CI, CI, I64, P, ctypes.c_float, P, P]),
+    ("aib_silu_mul_bf16", CI, [P, P, I64, I64, P]),
 ]
 
 

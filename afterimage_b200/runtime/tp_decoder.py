@@ -251,10 +251,14 @@ class TPDecoder:
     """One rank of a tensor-parallel decoder. `group` is a torch.distributed
     process group (None for a single rank)."""
 
-    def __init__(self, hf_cfg, weights: dict, world: int = 1, rank: int = 0, group=None, device="cuda"):
+    def __init__(self, hf_cfg, weights: dict, world: int = 1, rank: int = 0, group=None, device="cuda",
+                 fused: bool = True):
         self.cfg = hf_cfg
         self.world, self.rank, self.group = world, rank, group
         self.device = torch.device(device)
+        # single-token forwards use the fused layer kernels (csrc/tp_ops.cu); the torch
+        # layer math remains for prompts, and for CPU ranks (host-logic tests)
+        self.fused = bool(fused) and self.device.type == "cuda"
         self.H = hf_cfg.hidden_size
         self.hd = getattr(hf_cfg, "head_dim", None) or self.H // hf_cfg.num_attention_heads
         self.nh = hf_cfg.num_attention_heads // world
@@ -272,6 +276,54 @@ class TPDecoder:
         theta = rp.get("rope_theta", getattr(hf_cfg, "rope_theta", 10000.0))
         self.inv_freq = 1.0 / (theta ** (torch.arange(0, self.hd, 2, dtype=torch.int64).to(
             device=self.device, dtype=torch.float) / self.hd))
+        if self.fused:
+            self._join_resident()
+
+    # q/k/v (and gate/up) consume the same input: stored back to back they are one projection
+    JOINS = (("self_attn.qkv_proj.weight", ("self_attn.q_proj.weight", "self_attn.k_proj.weight",
+                                            "self_attn.v_proj.weight")),
+             ("mlp.gate_up_proj.weight", ("mlp.gate_proj.weight", "mlp.up_proj.weight")))
+
+    def _join_resident(self) -> None:
+        """Resident BF16 shards of q/k/v and of gate/up are moved into one
+        buffer each; the separate names stay as views of it."""
+        for i in range(self.n_layers):
+            p = "model.layers.%d." % i
+            for joined, names in self.JOINS:
+                parts = [self.w.get(p + n) for n in names]
+                if any(t is None or callable(t) or t.dim() != 2 for t in parts):
+                    continue
+                if len({t.shape[1] for t in parts}) != 1:
+                    continue
+                buf = torch.cat(parts, 0)
+                r = 0
+                for n, t in zip(names, parts):
+                    self.w[p + n] = buf[r:r + t.shape[0]]
+                    r += t.shape[0]
+                self.w[p + joined] = buf
+
+    @staticmethod
+    def _adjacent(parts: list) -> torch.Tensor | None:
+        """One [sum of rows, cols] view over 2-D tensors stored back to back
+        in one buffer, or None."""
+        first = parts[0]
+        cols = first.shape[1]
+        end = first.data_ptr()
+        for t in parts:
+            if t.dim() != 2 or t.shape[1] != cols or not t.is_contiguous() or t.dtype != first.dtype \
+                    or t.data_ptr() != end:
+                return None
+            end += t.numel() * t.element_size()
+        rows = sum(t.shape[0] for t in parts)
+        return torch.as_strided(first, (rows, cols), (cols, 1))
+
+    def _joined(self, W: dict, joined: str, names: tuple) -> torch.Tensor:
+        t = W.get(joined)
+        if t is not None:
+            return t
+        parts = [W[n] for n in names]
+        t = self._adjacent(parts)
+        return t if t is not None else torch.cat(parts, 0)
 
     # -- weights -----------------------------------------------------------
     def weight(self, key: str) -> torch.Tensor:
@@ -357,6 +409,39 @@ class TPDecoder:
         m = F.silu(F.linear(h, W["mlp.gate_proj.weight"])) * F.linear(h, W["mlp.up_proj.weight"])
         return x + self._all_reduce(F.linear(m, W["mlp.down_proj.weight"]))
 
+    def _layer_fused(self, i: int, W: dict, x: torch.Tensor, delta, cache: KVCache,
+                     pos: torch.Tensor) -> torch.Tensor:
+        """One layer for one token with the fused kernels. x [1, H] is the
+        residual stream, updated in place with the previous layer's pending
+        MLP output `delta`; returns this layer's (all-reduced) MLP output,
+        which the next norm adds. Same math as _layer_math."""
+        from . import tp_ops
+        h = tp_ops.add_rmsnorm(x, delta, W["input_layernorm.weight"], self.eps)
+        qkv = F.linear(h, self._joined(W, *self.JOINS[0]))
+        q = torch.empty(self.nh, 1, self.hd, dtype=x.dtype, device=x.device)
+        qn = W.get("self_attn.q_norm.weight") if self.qk_norm else None
+        kn = W.get("self_attn.k_norm.weight") if self.qk_norm else None
+        tp_ops.qk_rope_cache(qkv, 1, self.nh, self.nkv, self.hd, qn, kn, self.eps, self.inv_freq, pos, q,
+                             cache.k[i], cache.v[i])
+        a = tp_ops.decode_attention(q, cache.k[i], cache.v[i], self.nh, self.nkv, self.hd, pos, self.hd ** -0.5)
+        o = self._all_reduce(F.linear(a[None], W["self_attn.o_proj.weight"]))
+        h = tp_ops.add_rmsnorm(x, o, W["post_attention_layernorm.weight"], self.eps)
+        m = tp_ops.silu_mul(F.linear(h, self._joined(W, *self.JOINS[1])))
+        return self._all_reduce(F.linear(m, W["mlp.down_proj.weight"]))
+
+    def _layers_fused(self, x: torch.Tensor, cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
+        """Every layer for one token, then the final norm; returns the
+        normalised hidden state [1, H]."""
+        from . import tp_ops
+        delta = None
+        for i in range(self.n_layers):
+            W = self.layer_weights(i)
+            t0 = _mark(torch.cuda.current_stream(self.device)) if self.timeline is not None else None
+            delta = self._layer_fused(i, W, x, delta, cache, pos)
+            if t0 is not None:
+                self.timeline.append(("compute", i, t0, _mark(torch.cuda.current_stream(self.device))))
+        return tp_ops.add_rmsnorm(x, delta, self.weight("model.norm.weight"), self.eps)
+
     def embed(self, ids: torch.Tensor) -> torch.Tensor:
         e = self.w["model.embed_tokens.weight"]
         if callable(e):
@@ -372,6 +457,11 @@ class TPDecoder:
         T = ids.shape[0]
         self.begin_forward()
         x = self.embed(ids)
+        if self.fused and T == 1 and cache is not None and start < cache.max_len:
+            pos_t = torch.full((1,), start, dtype=torch.int64, device=self.device)
+            h = self._layers_fused(x.contiguous(), cache, pos_t)
+            cache.length = start + 1
+            return self._all_gather_last(self.head_logits(h))
         pos = torch.arange(start, start + T, device=self.device)
         cos, sin = self._rope(pos, x.dtype)
         for i in range(self.n_layers):
@@ -391,11 +481,14 @@ class TPDecoder:
         device, so the step can be captured and replayed as a CUDA graph."""
         self.begin_forward()
         x = F.embedding(st.ids, self.weight("model.embed_tokens.weight"))
-        cos, sin = self._rope(st.pos, x.dtype)
-        torch.le(st.arange, st.pos, out=st.mask)
-        for i in range(self.n_layers):
-            x = self._layer(i, x, cos, sin, st.cache, 0, static=st)
-        x = _rms_norm(x, self.weight("model.norm.weight"), self.eps)
+        if self.fused:
+            x = self._layers_fused(x, st.cache, st.pos)
+        else:
+            cos, sin = self._rope(st.pos, x.dtype)
+            torch.le(st.arange, st.pos, out=st.mask)
+            for i in range(self.n_layers):
+                x = self._layer(i, x, cos, sin, st.cache, 0, static=st)
+            x = _rms_norm(x, self.weight("model.norm.weight"), self.eps)
         logits = self._all_gather_last(self.head_logits(x))
         nxt = logits[-1].argmax(-1, keepdim=True)
         st.tokens.index_copy_(0, st.step, nxt)
@@ -611,8 +704,9 @@ class CompressedTPDecoder(TPDecoder):
     decoded on a side stream while layer i's projections run."""
 
     def __init__(self, hf_cfg, weights: dict, streams: dict, world=1, rank=0, group=None, device="cuda",
-                 mode: str = "compressed", slots: int = 3, head_block_rows: int = 16384, overlap: bool = False):
-        super().__init__(hf_cfg, weights, world, rank, group, device)
+                 mode: str = "compressed", slots: int = 3, head_block_rows: int = 16384, overlap: bool = False,
+                 fused: bool = True):
+        super().__init__(hf_cfg, weights, world, rank, group, device, fused=fused)
         if mode not in ("compressed", "streamed"):
             raise ValueError("mode must be 'compressed' or 'streamed'")
         self.dev = _device.cuda_device(device)
@@ -751,6 +845,13 @@ class CompressedTPDecoder(TPDecoder):
                 o = buf[off:off + ss.rows * ss.cols_decoded]
                 d[j] = self._desc(g, base, ss.elem_lo, o)
                 views[g.key[len(p):]] = (o.view(ss.rows, ss.cols_decoded), ss)
+            # q/k/v and gate/up decoded back to back: one projection each
+            for joined, names in self.JOINS:
+                parts = [views.get(n) for n in names]
+                if all(v is not None and v[1].col_lo == 0 and v[1].cols == v[1].cols_decoded for v in parts):
+                    t = self._adjacent([v[0] for v in parts])
+                    if t is not None:
+                        views[joined] = (t, None)
             plan = (d, views)
             self._desc_cache[key] = plan
         return plan
@@ -774,7 +875,7 @@ class CompressedTPDecoder(TPDecoder):
             self._release_image(slot, stream)
             W = {}
             for name, (o, ss) in views.items():
-                W[name] = o if (ss.col_lo == 0 and ss.cols == ss.cols_decoded) else \
+                W[name] = o if (ss is None or (ss.col_lo == 0 and ss.cols == ss.cols_decoded)) else \
                     o[:, ss.col_lo:ss.col_lo + ss.cols].contiguous()
         return W
 
@@ -934,4 +1035,4 @@ def load_tp_decoder(store_dir, hf_cfg, world: int = 1, rank: int = 0, group=None
     if keep_compressed:
         return CompressedTPDecoder(hf_cfg, weights, streams, world, rank, group, dev,
                                    mode="streamed" if resident == "streamed" else "compressed", **kw)
-    return TPDecoder(hf_cfg, weights, world, rank, group, dev)
+    return TPDecoder(hf_cfg, weights, world, rank, group, dev, fused=kw.get("fused", True))

@@ -197,6 +197,31 @@ int aib_decode_gemv_bf16_batch(const aib_gemv_desc *descs, int count, int32_t *d
 #define AIB_GEMV_SCRATCH_FLOATS (1 << 20)
 int aib_decode_gemv_bf16_batch_noalloc(const aib_gemv_desc *descs, int count, int32_t *d_status, void *stream);
 
+/* ------------------------------------------------------------------------
+ * Single-token step of the tensor-parallel decoder: the small operations
+ * between a layer's projections, fused. They replace the layer math the
+ * reference runs in transformers' Qwen3 / Llama modules around its hooks
+ * (afterimage/runtime/streaming_engine.py:1871-1915), with the same BF16
+ * rounding points. Row-major BF16 (uint16 bits), work on `stream`.
+ * ------------------------------------------------------------------------ */
+/* x <- bf16(x + delta) when delta is not NULL (in place), then
+ * out = bf16(weight * bf16(x * rsqrt(mean(x^2) + eps))) per row. */
+int aib_add_rmsnorm_bf16(void *x, const void *delta, const void *weight, void *out, int64_t rows, int64_t cols,
+                         float eps, void *stream);
+/* qkv [T, (nh + 2 nkv) * hd]: per-head RMSNorm of q and k (when both norm
+ * weights are given), rotary embedding at positions *pos0 + t (rotate-half,
+ * cos/sin of pos * inv_freq rounded to BF16); q -> q_out [nh, T, hd],
+ * k and v -> k_cache / v_cache [nkv, max_len, hd] at those positions. */
+int aib_qk_rope_cache_bf16(const void *qkv, int T, int nh, int nkv, int hd, const void *q_norm_w,
+                           const void *k_norm_w, float eps, const float *inv_freq, const int64_t *pos0, void *q_out,
+                           void *k_cache, void *v_cache, int64_t max_len, void *stream);
+/* One query per head (q [nh, hd]) over cache positions [0, *pos]; kv head =
+ * head / (nh / nkv); out [nh * hd]. max_len <= 8192. */
+int aib_decode_attention_bf16(const void *q, const void *k_cache, const void *v_cache, int nh, int nkv, int hd,
+                              int64_t max_len, const int64_t *pos, float scale, void *out, void *stream);
+/* gate_up [T, 2I] (gate then up per row) -> out [T, I] = bf16(bf16(silu(gate)) * up). */
+int aib_silu_mul_bf16(const void *gate_up, void *out, int64_t T, int64_t I, void *stream);
+
 /* Elementwise recombine of an already-decoded exponent field: replaces
  * recombine_exponent_and_sign_mantissa / _recombine
  * (afterimage/runtime/compressed_store.py:94-130). */

@@ -49,7 +49,8 @@ def stores(tmp_path_factory):
 @pytest.mark.parametrize("resident,kw", [("decoded", {}), ("compressed", {}),
                                          ("compressed", {"overlap": True, "head_block_rows": 500}),
                                          ("streamed", {}), ("streamed", {"slots": 3, "overlap": True}),
-                                         ("streamed", {"slots": 1, "head_block_rows": 1536})])
+                                         ("streamed", {"slots": 1, "head_block_rows": 1536}),
+                                         ("decoded", {"fused": False}), ("streamed", {"fused": False})])
 @pytest.mark.parametrize("which", ["ref", "tp_ready"])
 def test_tp_single_gpu_matches_transformers(stores, resident, kw, which):
     from afterimage_b200.runtime.tp_decoder import load_tp_decoder
@@ -71,7 +72,8 @@ def test_tp_single_gpu_matches_transformers(stores, resident, kw, which):
         dec.close()
 
 
-@pytest.mark.parametrize("resident,kw", [("decoded", {}), ("compressed", {}), ("compressed", {"overlap": True})])
+@pytest.mark.parametrize("resident,kw", [("decoded", {}), ("compressed", {}), ("compressed", {"overlap": True}),
+                                         ("decoded", {"fused": False}), ("compressed", {"fused": False})])
 def test_tp_graphed_generation(stores, resident, kw):
     """The single-token step captured as a CUDA graph (decode launches
     included) gives the greedy tokens of the eager decoder and of
@@ -114,7 +116,14 @@ def test_tp_decoded_weights_bit_exact(stores):
                 for i in range(cfg.num_hidden_layers):
                     W = dec.layer_weights(i)
                     for name, w in W.items():
-                        assert torch.equal(w.view(torch.int16), sd["model.layers.%d.%s" % (i, name)].view(torch.int16))
+                        key = "model.layers.%d.%s" % (i, name)
+                        if name in ("self_attn.qkv_proj.weight", "mlp.gate_up_proj.weight"):
+                            parts = ("q_proj", "k_proj", "v_proj") if "qkv" in name else ("gate_proj", "up_proj")
+                            pre = key.rsplit(".", 2)[0]
+                            want = torch.cat([sd["%s.%s.weight" % (pre, n)] for n in parts], 0)
+                        else:
+                            want = sd[key]
+                        assert torch.equal(w.view(torch.int16), want.view(torch.int16)), name
             if resident == "streamed":
                 dec.close()
 
