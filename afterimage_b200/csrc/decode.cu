@@ -17,14 +17,17 @@
 //     than that (rare: the table covers every code of <= 12 bits) take an
 //     exact slow path through the reference LUT in global memory, so every
 //     decoded symbol equals the reference's LUT result;
-//   * each lane streams its chunk's bytes through a register queue of
-//     16-byte aligned loads into a 64-bit bit buffer;
+//   * each lane's chunk bytes stream through a per-lane shared-memory ring
+//     of 16-byte blocks filled by cp.async a few blocks ahead; the 64-bit
+//     bit buffer refills 32-bit words straight from that ring;
 //   * symbols are flushed four at a time into a per-lane shared-memory
 //     ring; every 64 symbols the warp merges the ring with the sign/mantissa
 //     bytes (the reference's _recombine, compressed_store.py:94-114) and
 //     writes 16-byte vectorised BF16 stores, 128 contiguous bytes per chunk.
 // The decoder uses no tensor cores and no scratch global memory: the
-// exponent never round-trips through HBM.
+// exponent never round-trips through HBM. The fused decode -> GEMV kernels
+// further down share the reader and table; they keep one fp32 partial sum
+// per chunk in scratch.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
