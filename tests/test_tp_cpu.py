@@ -204,3 +204,38 @@ def test_tp_forward_matches_transformers_on_cpu(world, tie):
 
 
 PORTS = {(2, False): _free_port(), (2, True): _free_port()}
+
+
+def test_adjacent_views_join_back_to_back_projections():
+    """q/k/v (or gate/up) stored back to back form one [rows, cols] view;
+    anything else (gap, other buffer, other width) does not."""
+    buf = torch.arange(10 * 6, dtype=torch.float32).reshape(10, 6)
+    q, k, v = buf[:4], buf[4:7], buf[7:]
+    j = TPDecoder._adjacent([q, k, v])
+    assert j is not None and j.shape == (10, 6) and torch.equal(j, buf)
+    assert j.data_ptr() == buf.data_ptr()
+    assert TPDecoder._adjacent([q, buf[5:7]]) is None              # gap
+    assert TPDecoder._adjacent([q, torch.zeros(3, 6)]) is None     # other buffer
+    assert TPDecoder._adjacent([buf[:2, :3], buf[2:4, :3]]) is None  # not contiguous rows
+
+
+def test_engine_headroom_counts_inflight_layers():
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, engine_headroom_bytes, layer_working_set
+    from afterimage_b200.runtime.vram_planner import DEFAULT_ACTIVATION_SLACK_BYTES, decode_scratch_bytes
+    man = {"tensors": {
+        "model.embed_tokens.weight": {"orig_bytes": 900, "comp_bytes": 900, "row_gather": True},
+        "lm_head.weight": {"orig_bytes": 500, "comp_bytes": 350},
+        "model.layers.0.a.weight": {"orig_bytes": 100, "comp_bytes": 70},
+        "model.layers.0.b.weight": {"orig_bytes": 200, "comp_bytes": 140},
+        "model.layers.1.a.weight": {"orig_bytes": 120, "comp_bytes": 80},
+    }}
+    assert layer_working_set(man) == 100 + 70 + 200 + 140
+    scratch = decode_scratch_bytes(1 << 10) + DEFAULT_ACTIVATION_SLACK_BYTES
+    for k, want in ((1, 510), (2, 1020)):
+        cfg = EngineConfig(decode_slice_elems=1 << 10, max_inflight_layers=k)
+        assert engine_headroom_bytes(man, cfg) == want + scratch
+    # a chunked head materialises one block: the layers set the floor
+    cfg = EngineConfig(decode_slice_elems=1 << 10, max_inflight_layers=1)
+    assert engine_headroom_bytes(man, cfg, {"lm_head.weight": 50}) == 510 + scratch
+    assert engine_headroom_bytes({"tensors": {"lm_head.weight": {"orig_bytes": 5000, "comp_bytes": 1}}}, cfg) \
+        == 5000 + scratch
