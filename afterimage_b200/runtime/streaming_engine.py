@@ -441,6 +441,13 @@ class StreamingLosslessModel:
         self._pool = concurrent.futures.ThreadPoolExecutor(max_workers=max(1, depth), thread_name_prefix="aib-io")
         self._futures: dict[int, concurrent.futures.Future] = {}
         self._inflight: list = []   # (layer, compute-stream event after its forward), oldest first
+        self._head_future = None
+        self._head_reader = None
+        self._head_buf = None
+        if self._chunked_head_rows():
+            self._head_reader = BinaryWeightReader(self.store / "weights.bin", direct=self.config.direct_io,
+                                                   threads=self.config.io_threads)
+            self._head_buf = PinnedBuffer()
 
         self._materialize_resident()
         self._install_hooks()
@@ -703,12 +710,19 @@ class StreamingLosslessModel:
             _, ev = self._inflight.pop(0)
             ev.synchronize()
 
+    def _streams(self, idx: int) -> bool:
+        """Whether layer idx brings weights over PCIe (disk or RAM tier)."""
+        return any(self.tier_of(k) in ("disk", "ram") for k in self._layer_keys[idx])
+
     def _load_layer(self, idx: int) -> None:
-        self._bound_inflight(self.config.max_inflight_layers - 1)
+        if self._streams(idx):
+            self._bound_inflight(self.config.max_inflight_layers - 1)
         compute = torch.cuda.current_stream(self.device)
         arrays, slot = self._fetch_layer(idx)
         for ahead in range(1, self.config.io_prefetch_depth + 1):
             self._start_prefetch(idx + ahead)
+        if idx == max(0, self.n_layers - 2):
+            self._start_head_prefetch()
         to_decode: dict[str, ResidentLayer] = {}
         streamed = {k: _encoded_from_arrays(self.manifest["tensors"][k], a)
                     for k, a in arrays.items() if self.manifest["tensors"][k]["compressed"]}
@@ -743,9 +757,10 @@ class StreamingLosslessModel:
         self.stats.layer_loads += 1
 
     def _free_layer(self, idx: int) -> None:
-        ev = torch.cuda.Event()
-        ev.record(torch.cuda.current_stream(self.device))
-        self._inflight.append((idx, ev))
+        if self._streams(idx):
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(self.device))
+            self._inflight.append((idx, ev))
         for k in self._layer_keys[idx]:
             if self.tier_of(k) == "vram" and k not in self._vram_compressed:
                 continue
@@ -796,6 +811,16 @@ class StreamingLosslessModel:
         if chunked:
             self._install_chunked_lm_head()
 
+    def _start_head_prefetch(self) -> None:
+        """The chunked head's compressed bytes are read into their own
+        page-locked buffer while the last layers run (its block uploads
+        then copy by DMA). Its uploads finish before the head returns, so
+        the buffer is free again for the next forward."""
+        if self._head_reader is None or self._head_future is not None:
+            return
+        self._head_future = self._pool.submit(self._read_arrays, [self.CHUNKED_HEAD_KEY], self._head_reader,
+                                              self._head_buf)
+
     def _install_chunked_lm_head(self) -> None:
         """Logits in row blocks instead of a materialised lm_head (reference
         streaming_engine.py:2271-2334): logits[..., a:b] = x @ W[a:b].T, each
@@ -809,7 +834,9 @@ class StreamingLosslessModel:
 
         def forward(x: torch.Tensor) -> torch.Tensor:
             self._bound_inflight(0)
-            arrays = self._read_arrays([key], self._reader, pinned=False)[key]
+            fut, self._head_future = self._head_future, None
+            arrays = (fut.result() if fut is not None
+                      else self._read_arrays([key], self._head_reader, self._head_buf))[key]
             layer = _encoded_from_arrays(meta, arrays)
             parts = []
             for r0 in range(0, rows, step):
@@ -905,7 +932,7 @@ class StreamingLosslessModel:
             fut.cancel()
         self._futures.clear()
         self._pool.shutdown(wait=True)
-        for r in [self._reader] + self._slot_readers:
+        for r in [self._reader] + self._slot_readers + ([self._head_reader] if self._head_reader else []):
             r.close()
 
     def __enter__(self):
