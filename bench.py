@@ -462,6 +462,15 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
             shutil.rmtree(root, ignore_errors=True)
 
 
+def bench_config(args, spec, step_bytes: int, world: int) -> dict:
+    """The workload description both arms print (same keys and values)."""
+    return {"workload": args.workload, "tensors": [n for n, _, _ in spec],
+            "layer_weights": sum(r * c for _, r, c in spec),
+            "chunk_size": {"default": 1024, **WORKLOAD_CHUNKS.get(args.workload, {})},
+            "distinct_resident_layers": args.layers, "l2": "inputs > L2 (no flush needed)",
+            "algorithmic_bytes_per_step": step_bytes, "parallelism": f"replica{world}"}
+
+
 def dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -498,9 +507,8 @@ def run_reference(args, world, rank):
     line = {"metric": METRIC, "value": round(v, 4), "unit": "GB/s", "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
-            "data": "synthetic", "config": {"workload": args.workload,
-                                           "layer_weights": sum(r * c for _, r, c in spec),
-                                           "chunk_size": 1024, "sample_per_step": "q_proj tensor (5120x5120)"},
+            "data": "synthetic", "config": dict(bench_config(args, spec, int(nbytes), world),
+                                                sample_per_step="q_proj tensor (5120x5120)"),
             "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": "q_proj-shaped tensor per step; oracle port of the reference CPU decoder"},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -649,11 +657,7 @@ def main(argv=None) -> int:
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
             "data": "synthetic: random N(0,0.02) BF16 weights, seeded, encoded by afterimage_b200 (reference-identical)",
-            "config": {"workload": args.workload, "tensors": [n for n, _, _ in spec],
-                       "layer_weights": sum(r * c for _, r, c in spec),
-                       "chunk_size": {"default": 1024, **WORKLOAD_CHUNKS.get(args.workload, {})},
-                       "distinct_resident_layers": args.layers, "l2": "inputs > L2 (no flush needed)",
-                       "algorithmic_bytes_per_step": int(step_bytes[0]), "parallelism": f"replica{world}"},
+            "config": bench_config(args, spec, int(step_bytes[0]), world),
             "gpu_launches": args.steps * (-(-len(spec) // 16)),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
