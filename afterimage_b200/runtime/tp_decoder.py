@@ -683,6 +683,22 @@ def _fill_image(dst: np.ndarray, segs: list[_Seg]) -> None:
         dst[g.sm_off:g.sm_off + sm.shape[0]] = sm
 
 
+def plan_resident_layers(layer_bytes: list[int], vram_budget_bytes: int, fixed_bytes: int) -> list[int]:
+    """Which layer images a streamed rank keeps in HBM under a per-rank VRAM
+    budget: the residency planner (vram_planner.plan_tiers) run on this
+    rank's shard images, with the rank's fixed working set (slot ring,
+    decode outputs, head, tables, activations) as headroom. Raises if the
+    budget cannot hold the working set."""
+    from .vram_planner import TensorInfo, plan_tiers
+    infos = [TensorInfo(key="layer.%d" % i, orig_bytes=int(n), comp_bytes=int(n), is_layer_weight=True)
+             for i, n in enumerate(layer_bytes)]
+    plan = plan_tiers(infos, vram_budget_bytes / 1e9, 0.0, vram_headroom_bytes=int(fixed_bytes))
+    if not plan.feasible:
+        raise ValueError("per-rank VRAM budget %.2f GB is below this rank's streaming working set %.2f GB"
+                         % (vram_budget_bytes / 1e9, fixed_bytes / 1e9))
+    return sorted(int(k.split(".")[1]) for k in plan.vram_keys)
+
+
 class CompressedTPDecoder(TPDecoder):
     """TP decoder whose projection shards stay compressed; each layer's
     shards are decoded by one batched launch per forward, straight into
@@ -697,7 +713,10 @@ class CompressedTPDecoder(TPDecoder):
         buffers hold the next layers, filled by one copy per layer on a
         copy stream that runs ahead of the compute stream (layer i+slots
         uploads into layer i's buffer as soon as its decode has run), so
-        the PCIe transfer overlaps decode and projection.
+        the PCIe transfer overlaps decode and projection. With a per-rank
+        `vram_budget_gb`, the planner keeps as many layer images resident in
+        HBM as the budget allows beside that working set; only the rest
+        stream.
     The head (vocab rows of lm_head, or of a tied embedding) stays compressed
     in HBM and is decoded `head_block_rows` rows at a time into one reused
     buffer, so it never exists decoded in full. With `overlap`, layer i+1 is
@@ -705,7 +724,7 @@ class CompressedTPDecoder(TPDecoder):
 
     def __init__(self, hf_cfg, weights: dict, streams: dict, world=1, rank=0, group=None, device="cuda",
                  mode: str = "compressed", slots: int = 3, head_block_rows: int = 16384, overlap: bool = False,
-                 fused: bool = True):
+                 fused: bool = True, vram_budget_gb: float | None = None, max_context: int = 4096):
         super().__init__(hf_cfg, weights, world, rank, group, device, fused=fused)
         if mode not in ("compressed", "streamed"):
             raise ValueError("mode must be 'compressed' or 'streamed'")
@@ -747,27 +766,44 @@ class CompressedTPDecoder(TPDecoder):
             g = self.head[0]
             rows = min(self.head_block_rows, g.ss.rows)
             self._head_buf = torch.empty(rows * g.ss.cols_decoded, dtype=torch.bfloat16, device=self.dev)
-        if mode == "compressed":
-            self.images = []
-            for i in range(self.n_layers):
-                img = np.zeros(max(sizes[i], 16), dtype=np.uint8)
-                _fill_image(img, self.segs[i])
-                self.images.append(torch.from_numpy(img).to(self.dev))
-        else:
-            offs = np.concatenate([[0], np.cumsum([_up(max(n, 16)) for n in sizes])]).astype(np.int64)
+        resident = set(range(self.n_layers))
+        self.budget_plan = None
+        if mode == "streamed":
+            resident = set()
+            if vram_budget_gb is not None:
+                n_slots = max(1, slots)
+                fixed = (n_slots * _up(max(max(sizes), 16)) + sum(t.numel() * 2 for t in self._out_sets)
+                         + (self.head[1].numel() + self._head_buf.numel() * 2 if self.head is not None else 0)
+                         + sum(t.block.numel() + t.sym_lut.numel() * 4 + t.len_lut.numel()
+                               for t in self.tables.values())
+                         + 2 * self.n_layers * self.nkv * self.hd * 2 * max_context
+                         + (256 << 20))  # activations of a prompt pass, logits, allocator slack
+                resident = set(plan_resident_layers(sizes, int(vram_budget_gb * 1e9), fixed))
+                self.budget_plan = {"vram_budget_gb": vram_budget_gb, "fixed_bytes": int(fixed),
+                                    "resident_layers": len(resident), "streamed_layers": self.n_layers - len(resident)}
+        self.images = {}
+        for i in sorted(resident):
+            img = np.zeros(max(sizes[i], 16), dtype=np.uint8)
+            _fill_image(img, self.segs[i])
+            self.images[i] = torch.from_numpy(img).to(self.dev)
+        self.streamed = [i for i in range(self.n_layers) if i not in resident]
+        self._stream_pos = {layer: j for j, layer in enumerate(self.streamed)}
+        self.h2d_bytes = 0
+        self.host = {}
+        if self.streamed:
+            ssz = [_up(max(sizes[i], 16)) for i in self.streamed]
+            offs = np.concatenate([[0], np.cumsum(ssz)]).astype(np.int64)
             self.arena = HostArena(int(offs[-1]))
-            self.host = []
-            for i in range(self.n_layers):
-                view = self.arena.array[offs[i]:offs[i] + max(sizes[i], 16)]
+            for j, i in enumerate(self.streamed):
+                view = self.arena.array[offs[j]:offs[j] + max(sizes[i], 16)]
                 _fill_image(view, self.segs[i])
-                self.host.append(self.arena.tensor[offs[i]:offs[i] + max(sizes[i], 16)])
-            cap = _up(max(max(sizes), 16))
+                self.host[i] = self.arena.tensor[offs[j]:offs[j] + max(sizes[i], 16)]
+            cap = _up(max(max(sizes[i] for i in self.streamed), 16))
             self.slots = [torch.empty(cap, dtype=torch.uint8, device=self.dev) for _ in range(max(1, slots))]
             self.copy_stream = torch.cuda.Stream(self.dev)
             self._consumed = [None] * len(self.slots)
             self._pending: list = []      # (layer, slot, upload-done event), in upload order
             self._next_slot = 0
-            self.h2d_bytes = 0
 
     # -- streamed pipeline ---------------------------------------------------------
     def _issue_upload(self, layer: int) -> None:
@@ -789,14 +825,15 @@ class CompressedTPDecoder(TPDecoder):
 
     def _take_image(self, i: int) -> tuple[torch.Tensor, int, object]:
         """(device image holding layer i, slot id or -1, event to wait on)."""
-        if self.mode == "compressed":
+        if i in self.images:
             return self.images[i], -1, None
         if not self._pending or self._pending[0][0] != i:
             # out of step (first use, or a forward that stopped early): restart the ring at layer i
             self.copy_stream.synchronize()
             self._pending.clear()
-            for j in range(len(self.slots)):
-                self._issue_upload((i + j) % self.n_layers)
+            j0 = self._stream_pos[i]
+            for j in range(min(len(self.slots), len(self.streamed))):
+                self._issue_upload(self.streamed[(j0 + j) % len(self.streamed)])
         layer, slot, ev = self._pending.pop(0)
         return self.slots[slot], slot, ev
 
@@ -806,9 +843,8 @@ class CompressedTPDecoder(TPDecoder):
         done = torch.cuda.Event()
         done.record(stream)
         self._consumed[slot] = done
-        last = self._pending[-1][0] if self._pending else None
-        nxt = ((last if last is not None else -1) + 1) % self.n_layers
-        self._issue_upload(nxt)
+        last = self._pending[-1][0] if self._pending else self.streamed[-1]
+        self._issue_upload(self.streamed[(self._stream_pos[last] + 1) % len(self.streamed)])
 
     # -- decode ----------------------------------------------------------------
     @staticmethod
@@ -950,16 +986,17 @@ class CompressedTPDecoder(TPDecoder):
         return total
 
     def h2d_bytes_per_forward(self) -> int:
-        return sum(int(h.numel()) for h in self.host) if self.mode == "streamed" else 0
+        return sum(int(h.numel()) for h in self.host.values())
 
     def close(self) -> None:
         super().close()
-        if self.mode == "streamed":
+        if self.streamed:
             self.copy_stream.synchronize()
             torch.cuda.synchronize(self.dev)
             self.slots = []
-            self.host = []
+            self.host = {}
             self.arena.close()
+            self.streamed = []
 
 
 class HostRows:

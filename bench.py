@@ -379,6 +379,7 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
         prompt = torch.randint(0, cfg.vocab_size, (1, 64), generator=torch.Generator().manual_seed(64))
         seqs = {}
         for name, resident, kw in (("streamed", "streamed", {}),
+                                   ("streamed_4GB_per_rank", "streamed", {"vram_budget_gb": 4.0, "max_context": 128}),
                                    ("compressed_resident", "compressed", {"overlap": True})):
             t0 = time.perf_counter()
             dec = load_tp_decoder(store, cfg, world, rank, None, dev, resident=resident, **kw)
@@ -442,6 +443,8 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
                                    "note": "tokens_per_s includes the 64-token prompt pass (a captured graph "
                                            "too); step_ms is one replay of the captured single-token step"}
                 dec.release_graphs()
+            if getattr(dec, "budget_plan", None):
+                info["budget_plan"] = dec.budget_plan
             if resident == "streamed":
                 hb = dec.h2d_bytes_per_forward()
                 up = tl.get("upload_busy_ms", 0.0)
@@ -453,7 +456,7 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
             out[name] = info
             del dec, cache
             torch.cuda.empty_cache()
-        out["tokens_equal_across_modes"] = bool(torch.equal(seqs["streamed"], seqs["compressed_resident"]))
+        out["tokens_equal_across_modes"] = all(bool(torch.equal(v, seqs["compressed_resident"])) for v in seqs.values())
         out["all_reduce"] = allreduce_probe(world, dev, cfg.hidden_size, 2 * cfg.num_hidden_layers)
         return out
     finally:

@@ -239,3 +239,13 @@ def test_engine_headroom_counts_inflight_layers():
     assert engine_headroom_bytes(man, cfg, {"lm_head.weight": 50}) == 510 + scratch
     assert engine_headroom_bytes({"tensors": {"lm_head.weight": {"orig_bytes": 5000, "comp_bytes": 1}}}, cfg) \
         == 5000 + scratch
+
+
+def test_plan_resident_layers_fills_budget_beside_working_set():
+    from afterimage_b200.runtime.tp_decoder import plan_resident_layers
+    sizes = [100, 100, 100, 100]
+    assert plan_resident_layers(sizes, 1000, 500) == [0, 1, 2, 3]
+    assert plan_resident_layers(sizes, 750, 500) == [0, 1]
+    assert plan_resident_layers(sizes, 599, 500) == []
+    with pytest.raises(ValueError, match="working set"):
+        plan_resident_layers(sizes, 400, 500)

@@ -98,6 +98,35 @@ def test_tp_graphed_generation(stores, resident, kw):
     dec.close()
 
 
+def test_tp_streamed_under_a_per_rank_budget(stores):
+    """A per-rank VRAM budget keeps the layers the planner picks resident in
+    HBM and streams only the rest; weights and tokens are unchanged."""
+    from afterimage_b200.runtime.tp_decoder import load_tp_decoder
+    cfg, model, store, tp_store = stores
+    big = load_tp_decoder(tp_store, cfg, 1, 0, None, "cuda", resident="streamed", vram_budget_gb=100.0)
+    assert big.streamed == [] and big.h2d_bytes_per_forward() == 0
+    fixed = big.budget_plan["fixed_bytes"]
+    one = big.images[0].numel()
+    big.close()
+    dec = load_tp_decoder(tp_store, cfg, 1, 0, None, "cuda", resident="streamed",
+                          vram_budget_gb=(fixed + one + 1000) / 1e9)
+    assert sorted(dec.images) == [0] and dec.streamed == list(range(1, cfg.num_hidden_layers))
+    sd = {k: v.to("cuda") for k, v in model.state_dict().items()}
+    for rep in range(2):
+        for i in range(cfg.num_hidden_layers):
+            for name, w in dec.layer_weights(i).items():
+                if name in ("self_attn.qkv_proj.weight", "mlp.gate_up_proj.weight"):
+                    continue
+                assert torch.equal(w.view(torch.int16), sd["model.layers.%d.%s" % (i, name)].view(torch.int16))
+    model = model.to("cuda")
+    ids = torch.randint(0, cfg.vocab_size, (1, 7), device="cuda")
+    seq = dec.generate_greedy(ids, 4)
+    ref_seq, margins = _ref_greedy(model, ids, 4)
+    _check_greedy(seq, ref_seq, margins, 7)
+    assert dec.h2d_bytes_per_forward() == sum(int(h.numel()) for h in dec.host.values()) > 0
+    dec.close()
+
+
 def _lib_status_clear():
     from afterimage_b200.runtime import _device
     _device.check_status(torch.device("cuda", torch.cuda.current_device()))
