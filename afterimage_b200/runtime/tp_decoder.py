@@ -25,7 +25,6 @@ from __future__ import annotations
 
 import dataclasses
 import json
-import math
 import pathlib
 
 import numpy as np
@@ -755,7 +754,6 @@ class CompressedTPDecoder(TPDecoder):
         # decoded weights land in preallocated output sets (two when the decode of layer
         # i+1 overlaps layer i's projections), so descriptors are built once per
         # (layer, image, set) and nothing is allocated per layer
-        self._views: list = []
         per_layer = [self._out_layout(segs) for segs in self.segs]
         set_elems = max([n for _, n in per_layer] + [1])
         self._out_sets = [torch.empty(set_elems, dtype=torch.bfloat16, device=self.dev)
