@@ -983,6 +983,12 @@ class CompressedTPDecoder(TPDecoder):
             total += n + g.packed_n + 4 * g.n_chunks + 32768 + 2 * n
         return total
 
+    def weights_per_forward(self) -> int:
+        """Weights one forward's projections read on this rank (decoded
+        elements of every layer shard and of the head shard)."""
+        segs = [g for layer in self.segs for g in layer] + ([self.head[0]] if self.head is not None else [])
+        return sum(g.ss.rows * g.ss.cols_decoded for g in segs)
+
     def h2d_bytes_per_forward(self) -> int:
         return sum(int(h.numel()) for h in self.host.values())
 

@@ -51,7 +51,7 @@ WORKLOADS = {"qwen3-14b-layer": QWEN3_14B_LAYER, "config1-4096x4096": CONFIG1,
 # whole chunks of every rank's columns)
 WORKLOAD_CHUNKS = {"qwen3-14b-layer-tp8": {"o_proj": 640, "down_proj": 1088}}
 FAST_TABLE_BYTES = 4096 * 8
-# BASELINE configs 2 and 4 (Qwen3 0.6B / 14B shapes), random-init weights
+# the benchmark's Qwen3-0.6B- and Qwen3-14B-shaped decoder configurations, random-init weights
 QWEN3_06B = dict(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
                  num_attention_heads=16, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
                  tie_word_embeddings=True, max_position_embeddings=4096)
@@ -59,6 +59,9 @@ QWEN3_14B = dict(vocab_size=151936, hidden_size=5120, intermediate_size=17408, n
                  num_attention_heads=40, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
                  tie_word_embeddings=False, max_position_embeddings=4096)
 METRIC = "bit-exact BF16 weight decode GB/s"
+# host -> device copy rate of one B200 (PCIe 5 x16) measured on this pool: pinned copies of
+# hundreds of MB reach 55 GB/s (bench timelines, "h2d_gbps_in_step")
+PCIE_GBS = 55.0
 
 
 def env_int(name, default):
@@ -215,9 +218,10 @@ def synthetic_checkpoint(hf_cfg, seed: int, device):
 
 
 def run_tokens(args, dev) -> dict:
-    """tokens/s of greedy decoding on the Qwen3-14B shape (BASELINE config
-    4): the compressed store streamed under a 4 GB VRAM budget, the whole
-    model compressed-resident in HBM, and draft speculation with a
+    """tokens/s of greedy decoding on the Qwen3-14B shape (the benchmark's
+    streamed 14B configuration) through the transformers-driven engine: the
+    compressed store streamed under a 4 GB VRAM budget, the whole model
+    compressed-resident in HBM, and draft speculation with a
     Qwen3-0.6B-shaped draft at temperature 0 (token-identical to greedy)."""
     import shutil
     from transformers import AutoModelForCausalLM, Qwen3Config
@@ -346,7 +350,7 @@ def allreduce_probe(world: int, dev, hidden: int, count: int) -> dict | None:
 
 
 def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
-    """Greedy tokens/s of the Qwen3-14B shape through
+    """Greedy tokens/s of the Qwen3-14B shape (the benchmark's 14B configuration) through
     the tensor-parallel decoder on `world` GPUs (one rank per GPU; world=1
     is a single GPU): every rank decodes only its own column/row shards of
     every layer, one NCCL all-reduce after o_proj and after down_proj.
@@ -419,6 +423,16 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
                     "decode_bytes_per_forward_per_rank": dbytes,
                     "decode_gbps_in_step": round(dbytes / (dec_ms / 1e3) / 1e9, 1) if dec_ms else None,
                     "decode_hbm_frac": round(dbytes / (dec_ms / 1e3) / 1e9 / peak_hbm, 4) if dec_ms else None}
+            # the terms that bound one single-token forward on this rank: PCIe for the
+            # streamed bytes, HBM for the decode, HBM for the projections reading the
+            # decoded BF16 weights; the largest is the tokens/s roofline
+            terms = {"pcie_ms": round(dec.h2d_bytes_per_forward() / PCIE_GBS / 1e6, 3),
+                     "decode_hbm_ms": round(dbytes / peak_hbm / 1e6, 3),
+                     "projection_hbm_ms": round(2 * dec.weights_per_forward() / peak_hbm / 1e6, 3)}
+            bound = max(terms, key=terms.get)
+            info["roofline_terms"] = dict(terms, bound=bound, pcie_gbs=PCIE_GBS, hbm_gbs=peak_hbm,
+                                          step_ms=round(step_ms, 3),
+                                          frac_of_bound=round(terms[bound] / step_ms, 4) if step_ms else None)
             if resident != "streamed":
                 # the single-token step captured once as a CUDA graph and replayed per token
                 dec.generate_greedy_graphed(prompt, args.new_tokens)  # warm + capture

@@ -162,7 +162,7 @@ def test_gpu_bf16_scales_and_specials(scale):
 
 
 def test_config1_recipe_encoder_digests_and_gpu_roundtrip():
-    """BASELINE config 1 at full size: product encoder == reference encoder
+    """The single-tensor round-trip case (4096x4096, seed 0) at full size: product encoder == reference encoder
     (sha256 of every array), GPU decode == input, bit for bit."""
     from afterimage_b200.runtime.compressed_store import compress_layer, decompress_layer_gpu
     c = G.case("config1_4096x4096")
