@@ -349,6 +349,15 @@ def allreduce_probe(world: int, dev, hidden: int, count: int) -> dict | None:
             "note": "one token's hidden state per all-reduce: latency-bound, far below link bandwidth"}
 
 
+def tp_store_chunk_size(world: int) -> int:
+    """Chunk size of the store written for a TP degree. A chunk is decoded
+    serially by one lane, so a rank's small layer shard is latency-bound on
+    its chunk length. Measured on B200 for one TP-8 rank's 14B layer: 85 us
+    at 1024 symbols, 75 at 512, 52 at 256. A whole layer is fastest at the
+    reference's 1024 (270 us; 350 at 256)."""
+    return 256 if world >= 8 else (512 if world >= 4 else 1024)
+
+
 def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
     """Greedy tokens/s of the Qwen3-14B shape (the benchmark's 14B configuration) through
     the tensor-parallel decoder on `world` GPUs (one rank per GPU; world=1
@@ -373,12 +382,15 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
            "new_tokens": args.new_tokens}
     try:
         if rank == 0:
+            from afterimage_b200.runtime.streaming_engine import tp_chunk_size
+            cs = tp_store_chunk_size(world)
             t0 = time.perf_counter()
-            m = write_store(synthetic_checkpoint(cfg, 14, dev), store, EngineConfig(chunk_size=1024), tied=False,
+            m = write_store(synthetic_checkpoint(cfg, 14, dev), store, EngineConfig(chunk_size=cs), tied=False,
                             model_id="synthetic/qwen3-14b-shape", progress_every=0, tp_row_chunks=8)
             out.update(store_gb=round(m["total_comp_bytes"] / 1e9, 2), ratio=round(m["ratio"], 4),
                        store_build_s=round(time.perf_counter() - t0, 1),
-                       store_chunking="chunk_size 1024; o_proj 640, down_proj 1088 (whole chunks per rank up to TP 8)")
+                       store_chunking="chunk_size %d; o_proj %d, down_proj %d (whole chunks per rank up to TP 8)"
+                       % (cs, tp_chunk_size(cfg.hidden_size, 8, cs), tp_chunk_size(cfg.intermediate_size, 8, cs)))
         _barrier(world)
         prompt = torch.randint(0, cfg.vocab_size, (1, 64), generator=torch.Generator().manual_seed(64))
         seqs = {}
