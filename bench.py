@@ -355,7 +355,7 @@ def tp_store_chunk_size(world: int) -> int:
     its chunk length. Measured on B200 for one TP-8 rank's 14B layer: 85 us
     at 1024 symbols, 75 at 512, 52 at 256. A whole layer is fastest at the
     reference's 1024 (270 us; 350 at 256)."""
-    return 256 if world >= 8 else (512 if world >= 4 else 1024)
+    return 256 if world >= 8 else 1024
 
 
 def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
