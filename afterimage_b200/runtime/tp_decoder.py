@@ -513,7 +513,8 @@ class TPDecoder:
         st = self._graph_state
         if st is None or st.max_len < P + max_new_tokens:
             self.release_graphs()
-            st = _StepState(self, max(128, P + max_new_tokens))
+            # 64 positions of room past the generation for replay_steps to continue it
+            st = _StepState(self, max(128, P + max_new_tokens + 64))
             self._graph_state = st
         pre = st.prefill.get(P)
         if pre is None:

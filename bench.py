@@ -58,6 +58,20 @@ QWEN3_06B = dict(vocab_size=151936, hidden_size=1024, intermediate_size=3072, nu
 QWEN3_14B = dict(vocab_size=151936, hidden_size=5120, intermediate_size=17408, num_hidden_layers=40,
                  num_attention_heads=40, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
                  tie_word_embeddings=False, max_position_embeddings=4096)
+LLAMA3_8B = dict(vocab_size=128256, hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                 num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=500000.0,
+                 tie_word_embeddings=False, max_position_embeddings=8192)
+MISTRAL_24B = dict(vocab_size=131072, hidden_size=5120, intermediate_size=32768, num_hidden_layers=40,
+                   num_attention_heads=32, num_key_value_heads=8, head_dim=128, rope_theta=1e8,
+                   tie_word_embeddings=False, max_position_embeddings=8192)
+# the benchmark's decoder configurations: config class, shape, prompt length, forced greedy
+# tokens and the VRAM budget of its streamed run
+MODELS = {
+    "qwen3-0.6b": ("Qwen3Config", QWEN3_06B, 64, 4, 1.0, "Qwen3-0.6B shape"),
+    "llama3-8b": ("LlamaConfig", LLAMA3_8B, 128, 8, 4.0, "Llama-3-8B shape"),
+    "qwen3-14b": ("Qwen3Config", QWEN3_14B, 64, 4, 4.0, "Qwen3-14B shape"),
+    "mistral-24b": ("MistralConfig", MISTRAL_24B, 256, 4, 8.0, "Mistral-Small-24B shape"),
+}
 METRIC = "bit-exact BF16 weight decode GB/s"
 # host -> device copy rate of one B200 (PCIe 5 x16) measured on this pool: pinned copies of
 # hundreds of MB reach 55 GB/s (bench timelines, "h2d_gbps_in_step")
@@ -217,34 +231,45 @@ def synthetic_checkpoint(hf_cfg, seed: int, device):
         yield name, t.cpu()
 
 
+def model_config(name: str):
+    import transformers
+    cls, shape, prompt, new, budget, label = MODELS[name]
+    return getattr(transformers, cls)(**shape), prompt, new, budget, label
+
+
 def run_tokens(args, dev) -> dict:
-    """tokens/s of greedy decoding on the Qwen3-14B shape (the benchmark's
-    streamed 14B configuration) through the transformers-driven engine: the
-    compressed store streamed under a 4 GB VRAM budget, the whole model
-    compressed-resident in HBM, and draft speculation with a
-    Qwen3-0.6B-shaped draft at temperature 0 (token-identical to greedy)."""
+    """tokens/s of greedy decoding on the --model shape (default the Qwen3-14B
+    shape, the benchmark's streamed 14B configuration) through the
+    transformers-driven engine: the compressed store streamed under the
+    configuration's VRAM budget (4 GB for 14B), the whole model
+    compressed-resident in HBM, and, for the 14B shape, draft speculation
+    with a Qwen3-0.6B-shaped draft at temperature 0 (token-identical to
+    greedy)."""
     import shutil
     from transformers import AutoModelForCausalLM, Qwen3Config
     from afterimage_b200.runtime.streaming_engine import EngineConfig, StreamingLosslessModel, write_store
     root = pathlib.Path(tempfile.mkdtemp(prefix="aib_tokens_", dir="/dev/shm" if os.path.isdir("/dev/shm") else None))
     try:
-        cfg = Qwen3Config(**QWEN3_14B)
+        cfg, P, new_default, budget, label = model_config(args.model)
+        new_tokens = args.new_tokens or new_default
+        args = argparse.Namespace(**{**vars(args), "new_tokens": new_tokens})
+        tied = bool(getattr(cfg, "tie_word_embeddings", False))
         t0 = time.perf_counter()
-        m = write_store(synthetic_checkpoint(cfg, 14, dev), root / "qwen3-14b", EngineConfig(chunk_size=1024),
-                        tied=False, model_id="synthetic/qwen3-14b-shape", progress_every=0)
+        m = write_store(synthetic_checkpoint(cfg, 14, dev), root / args.model, EngineConfig(chunk_size=1024),
+                        tied=tied, model_id="synthetic/%s-shape" % args.model, progress_every=0)
         build_s = time.perf_counter() - t0
         gen = torch.Generator().manual_seed(64)
-        prompt = torch.randint(0, cfg.vocab_size, (1, 64), generator=gen)
-        out = {"model": "Qwen3-14B shape, random N(0,0.02)", "params_orig_gb": round(m["total_orig_bytes"] / 1e9, 2),
+        prompt = torch.randint(0, cfg.vocab_size, (1, P), generator=gen)
+        out = {"model": label + ", random N(0,0.02)", "params_orig_gb": round(m["total_orig_bytes"] / 1e9, 2),
                "store_gb": round(m["total_comp_bytes"] / 1e9, 2), "ratio": round(m["ratio"], 4),
-               "store_build_s": round(build_s, 1), "prompt_tokens": 64, "new_tokens": args.new_tokens}
+               "store_build_s": round(build_s, 1), "prompt_tokens": P, "new_tokens": args.new_tokens}
         ref_tokens = None
-        for name, ecfg in (("streamed_4GB", EngineConfig(vram_budget_gb=4.0, io_prefetch_depth=4,
-                                                          lm_head_slice_rows=16384)),
+        for name, ecfg in (("streamed_%gGB" % budget, EngineConfig(vram_budget_gb=budget, io_prefetch_depth=4,
+                                                                   lm_head_slice_rows=0 if tied else 16384)),
                            ("resident_compressed", EngineConfig(vram_budget_gb=100.0, vram_tier_format="compressed"))):
             torch.cuda.empty_cache()
             torch.cuda.reset_peak_memory_stats(dev)
-            with StreamingLosslessModel("synthetic/qwen3-14b-shape", root / "qwen3-14b", device=str(dev),
+            with StreamingLosslessModel("synthetic/%s-shape" % args.model, root / args.model, device=str(dev),
                                         config=ecfg, hf_config=cfg) as eng:
                 eng.generate_greedy(prompt, 1)  # warm: kernels, tables, allocator
                 eng.stats.reset()
@@ -266,7 +291,7 @@ def run_tokens(args, dev) -> dict:
                     ref_tokens = seq
                 else:
                     out[name]["tokens_equal_streamed"] = bool(torch.equal(seq.cpu(), ref_tokens.cpu()))
-                if name == "resident_compressed":
+                if name == "resident_compressed" and args.model == "qwen3-14b":
                     dcfg = Qwen3Config(**QWEN3_06B)
                     draft = AutoModelForCausalLM.from_config(dcfg, dtype=torch.bfloat16).to(dev).eval()
                     eng.generate_speculative(prompt, 1, draft, k=8, temperature=0.0)
@@ -359,7 +384,7 @@ def tp_store_chunk_size(world: int) -> int:
 
 
 def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
-    """Greedy tokens/s of the Qwen3-14B shape (the benchmark's 14B configuration) through
+    """Greedy tokens/s of the --model shape (default Qwen3-14B, the benchmark's 14B configuration) through
     the tensor-parallel decoder on `world` GPUs (one rank per GPU; world=1
     is a single GPU): every rank decodes only its own column/row shards of
     every layer, one NCCL all-reduce after o_proj and after down_proj.
@@ -369,33 +394,35 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
       compressed_resident: compressed shards resident in HBM, decoded per
                            layer per forward, the next layer's decode
                            overlapping this layer's projections.
-    Timed: prompt (64 uniform ids) + new_tokens greedy tokens, CUDA events,
+    Timed: prompt (P uniform ids, 64 for 14B) + new_tokens greedy tokens, CUDA events,
     max over ranks. The store is written once (rank 0, TP-ready chunking)."""
-    from transformers import Qwen3Config
     from afterimage_b200.runtime.streaming_engine import EngineConfig, write_store
     from afterimage_b200.runtime.tp_decoder import KVCache, load_tp_decoder, timeline_summary, _mark
     import shutil
-    cfg = Qwen3Config(**QWEN3_14B)
+    cfg, P, new_default, budget, label = model_config(args.model)
+    args = argparse.Namespace(**{**vars(args), "new_tokens": args.new_tokens or new_default})
+    tied = bool(getattr(cfg, "tie_word_embeddings", False))
     root = _shared_tmpdir(world, rank, "aib_tp_")
-    store = root / "qwen3-14b-tp8"
-    out = {"model": "Qwen3-14B shape, random N(0,0.02)", "tp": world, "prompt_tokens": 64,
+    store = root / (args.model + "-tp8")
+    out = {"model": label + ", random N(0,0.02)", "tp": world, "prompt_tokens": P,
            "new_tokens": args.new_tokens}
     try:
         if rank == 0:
             from afterimage_b200.runtime.streaming_engine import tp_chunk_size
             cs = tp_store_chunk_size(world)
             t0 = time.perf_counter()
-            m = write_store(synthetic_checkpoint(cfg, 14, dev), store, EngineConfig(chunk_size=cs), tied=False,
-                            model_id="synthetic/qwen3-14b-shape", progress_every=0, tp_row_chunks=8)
+            m = write_store(synthetic_checkpoint(cfg, 14, dev), store, EngineConfig(chunk_size=cs), tied=tied,
+                            model_id="synthetic/%s-shape" % args.model, progress_every=0, tp_row_chunks=8)
             out.update(store_gb=round(m["total_comp_bytes"] / 1e9, 2), ratio=round(m["ratio"], 4),
                        store_build_s=round(time.perf_counter() - t0, 1),
                        store_chunking="chunk_size %d; o_proj %d, down_proj %d (whole chunks per rank up to TP 8)"
                        % (cs, tp_chunk_size(cfg.hidden_size, 8, cs), tp_chunk_size(cfg.intermediate_size, 8, cs)))
         _barrier(world)
-        prompt = torch.randint(0, cfg.vocab_size, (1, 64), generator=torch.Generator().manual_seed(64))
+        prompt = torch.randint(0, cfg.vocab_size, (1, P), generator=torch.Generator().manual_seed(64))
         seqs = {}
         for name, resident, kw in (("streamed", "streamed", {}),
-                                   ("streamed_4GB_per_rank", "streamed", {"vram_budget_gb": 4.0, "max_context": 128}),
+                                   ("streamed_%gGB_per_rank" % budget, "streamed",
+                                    {"vram_budget_gb": budget, "max_context": P + args.new_tokens + 8}),
                                    ("compressed_resident", "compressed", {"overlap": True})):
             t0 = time.perf_counter()
             dec = load_tp_decoder(store, cfg, world, rank, None, dev, resident=resident, **kw)
@@ -414,12 +441,12 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
             peak = _max_over_ranks(torch.cuda.max_memory_allocated(dev) / 1e9, world, dev)
             seqs[name] = seq.cpu()
             # one single-token forward with the event timeline (after the timed region)
-            cache = KVCache(dec.n_layers, dec.nkv, dec.hd, 80, dec.device)
+            cache = KVCache(dec.n_layers, dec.nkv, dec.hd, P + 16, dec.device)
             dec.forward(prompt, cache)
             torch.cuda.synchronize()
             dec.timeline = []
             base = _mark(torch.cuda.current_stream(dev))
-            dec.forward(seq[:, 64:65], cache)
+            dec.forward(seq[:, P:P + 1], cache)
             torch.cuda.synchronize()
             tl = timeline_summary(dec.timeline, base)
             dec.timeline = None
@@ -466,7 +493,7 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
                                    "s_per_token": round(gms / 1e3 / args.new_tokens, 4),
                                    "tokens_equal_eager": bool(torch.equal(gseq.cpu(), seqs[name])),
                                    "step_ms": round(sms, 3), "step_tokens_per_s": round(1e3 / sms, 2),
-                                   "note": "tokens_per_s includes the 64-token prompt pass (a captured graph "
+                                   "note": "tokens_per_s includes the %d-token prompt pass (a captured graph " % P +
                                            "too); step_ms is one replay of the captured single-token step"}
                 dec.release_graphs()
             if getattr(dec, "budget_plan", None):
@@ -558,10 +585,15 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--tokens", action="store_true",
-                    help="also measure greedy tokens/s on a Qwen3-14B-shaped model (builds a ~20 GB store)")
-    ap.add_argument("--new-tokens", type=int, default=4)
+                    help="also measure greedy tokens/s through the engine on the --model shape "
+                         "(the default Qwen3-14B shape builds a ~20 GB store)")
+    ap.add_argument("--new-tokens", type=int, default=None,
+                    help="greedy tokens per generation (default: the model configuration's)")
+    ap.add_argument("--model", default="qwen3-14b", choices=sorted(MODELS),
+                    help="decoder configuration of the tokens/s measurements")
     ap.add_argument("--no-tp-tokens", action="store_true",
-                    help="skip the tensor-parallel tokens/s measurement (builds a ~20 GB store in /dev/shm)")
+                    help="skip the tensor-parallel tokens/s measurement (its store of the --model shape "
+                         "is written to /dev/shm)")
     args = ap.parse_args(argv)
     args.warmup = max(3, args.warmup)
 
@@ -698,9 +730,9 @@ def main(argv=None) -> int:
             "cpu_baseline": cpu,
         }
         if tp_tokens is not None:
-            line["tokens_qwen3_14b_tp"] = tp_tokens
+            line["tokens_%s_tp" % args.model.replace("-", "_").replace(".", "")] = tp_tokens
         if tokens is not None:
-            line["tokens_per_s_qwen3_14b"] = tokens
+            line["tokens_per_s_%s" % args.model.replace("-", "_").replace(".", "")] = tokens
         print(json.dumps(line), flush=True)
     if world > 1:
         torch.distributed.destroy_process_group()
