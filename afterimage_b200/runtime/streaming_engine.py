@@ -785,26 +785,52 @@ class StreamingLosslessModel:
             layer.register_forward_hook(make_post(i), with_kwargs=True)
         self._install_streamed_module_hooks()
 
+    def _load_whole(self, key: str) -> torch.Tensor:
+        """One disk- or RAM-tier tensor outside the decoder layers, whole on
+        the device for one use: decoded from the store, from its compressed
+        pinned copy, or copied from its pinned BF16 copy."""
+        if self.tier_of(key) == "ram":
+            cached = self._ram_cache[key]
+            if isinstance(cached, CompressedLayer):
+                return decompress_layer_gpu(cached, device=self.device,
+                                            max_slice_elems=self.config.decode_slice_elems,
+                                            reuse_decode_tables=self.config.reuse_decode_tables)
+            return cached.to(self.device, non_blocking=True)
+        return self._decode_whole(key, self._read_arrays([key], self._reader, pinned=False)[key])
+
     def _install_streamed_module_hooks(self) -> None:
-        """Non-layer tensors that the plan leaves on disk (e.g. lm_head at a
-        small budget) are decoded just before their module runs."""
+        """Non-layer tensors that the plan leaves on disk or in host RAM (e.g.
+        lm_head, or a tied embedding, at a small budget) are loaded just
+        before their module runs and dropped after it (reference
+        streaming_engine.py:1952-2091).
+
+        A tied checkpoint stores only the embedding. When that streams, the
+        embedding module's post-hook swaps its parameter for a fresh meta
+        placeholder, so lm_head cannot share it: the head loads the same
+        stored tensor again for its own live range. (A meta weight given to
+        F.linear does not raise; it yields uninitialised logits.)"""
         groups: dict[str, list[str]] = {}
         chunked = self.CHUNKED_HEAD_KEY if self._chunked_head_rows() else None
         for key, tier in self._tier.items():
-            if tier == "disk" and not key.startswith("model.layers.") and key != chunked:
+            if tier in ("disk", "ram") and not key.startswith("model.layers.") and key != chunked:
                 groups.setdefault(key.rpartition(".")[0], []).append(key)
+        embed_key = "model.embed_tokens.weight"
+        if (bool(getattr(self.hf_cfg, "tie_word_embeddings", False))
+                and "lm_head.weight" not in self.manifest["tensors"]
+                and self._tier.get(embed_key) in ("disk", "ram")):
+            groups.setdefault("lm_head", []).append(("lm_head.weight", embed_key))
         for mod_name, keys in groups.items():
             mod = self.model.get_submodule(mod_name)
+            pairs = [k if isinstance(k, tuple) else (k, k) for k in keys]
 
-            def pre(module, args, keys=keys):
+            def pre(module, args, pairs=pairs):
                 self._bound_inflight(0)
-                arrays = self._read_arrays(keys, self._reader, pinned=False)
-                for k in keys:
-                    _set_param(self.model, k, self._decode_whole(k, arrays[k]))
+                for dst, src in pairs:
+                    _set_param(self.model, dst, self._load_whole(src))
 
-            def post(module, args, output, keys=keys):
-                for k in keys:
-                    _to_meta(self.model, k)
+            def post(module, args, output, pairs=pairs):
+                for dst, _ in pairs:
+                    _to_meta(self.model, dst)
                 return output
             mod.register_forward_pre_hook(pre)
             mod.register_forward_hook(post)

@@ -776,6 +776,10 @@ class CompressedTPDecoder(TPDecoder):
                          + sum(t.block.numel() + t.sym_lut.numel() * 4 + t.len_lut.numel()
                                for t in self.tables.values())
                          + 2 * self.n_layers * self.nkv * self.hd * 2 * max_context
+                         # device-resident tensors outside the layers (a tied embedding, norms)
+                         + sum(t.numel() * t.element_size() for k, t in self.w.items()
+                               if isinstance(t, torch.Tensor) and t.device.type == "cuda"
+                               and not k.startswith("model.layers."))
                          + (256 << 20))  # activations of a prompt pass, logits, allocator slack
                 resident = set(plan_resident_layers(sizes, int(vram_budget_gb * 1e9), fixed))
                 self.budget_plan = {"vram_budget_gb": vram_budget_gb, "fixed_bytes": int(fixed),

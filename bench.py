@@ -269,6 +269,7 @@ def run_tokens(args, dev) -> dict:
                            ("resident_compressed", EngineConfig(vram_budget_gb=100.0, vram_tier_format="compressed"))):
             torch.cuda.empty_cache()
             torch.cuda.reset_peak_memory_stats(dev)
+            harness = torch.cuda.memory_allocated(dev)  # the harness's own buffers, not the engine's
             with StreamingLosslessModel("synthetic/%s-shape" % args.model, root / args.model, device=str(dev),
                                         config=ecfg, hf_config=cfg) as eng:
                 eng.generate_greedy(prompt, 1)  # warm: kernels, tables, allocator
@@ -286,7 +287,8 @@ def run_tokens(args, dev) -> dict:
                              "io_s": round(st.io_seconds, 3), "h2d_enqueue_s": round(st.h2d_seconds, 3),
                              "decode_enqueue_s": round(st.decode_seconds, 3),
                              "vram_budget_gb": ecfg.vram_budget_gb,
-                             "peak_vram_gb": round(torch.cuda.max_memory_allocated(dev) / 1e9, 2)}
+                             "peak_vram_gb": round((torch.cuda.max_memory_allocated(dev) - harness) / 1e9, 2),
+                             "harness_vram_gb": round(harness / 1e9, 2)}
                 if ref_tokens is None:
                     ref_tokens = seq
                 else:
@@ -424,6 +426,7 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
                                    ("streamed_%gGB_per_rank" % budget, "streamed",
                                     {"vram_budget_gb": budget, "max_context": P + args.new_tokens + 8}),
                                    ("compressed_resident", "compressed", {"overlap": True})):
+            harness = torch.cuda.memory_allocated(dev)  # the harness's own buffers, not the decoder's
             t0 = time.perf_counter()
             dec = load_tp_decoder(store, cfg, world, rank, None, dev, resident=resident, **kw)
             torch.cuda.synchronize()
@@ -438,7 +441,7 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
             b.record()
             torch.cuda.synchronize()
             ms = _max_over_ranks(a.elapsed_time(b), world, dev)
-            peak = _max_over_ranks(torch.cuda.max_memory_allocated(dev) / 1e9, world, dev)
+            peak = _max_over_ranks((torch.cuda.max_memory_allocated(dev) - harness) / 1e9, world, dev)
             seqs[name] = seq.cpu()
             # one single-token forward with the event timeline (after the timed region)
             cache = KVCache(dec.n_layers, dec.nkv, dec.hd, P + 16, dec.device)
@@ -458,6 +461,7 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
             info = {"tokens_per_s": round(args.new_tokens / (ms / 1e3), 3),
                     "s_per_token": round(ms / 1e3 / args.new_tokens, 4), "load_s": round(load_s, 1),
                     "peak_vram_gb_per_rank": round(peak, 2),
+                    "harness_vram_gb_rank0": round(harness / 1e9, 2),
                     "decode_step_ms": round(step_ms, 3), "timeline_rank0": tl,
                     "decode_bytes_per_forward_per_rank": dbytes,
                     "decode_gbps_in_step": round(dbytes / (dec_ms / 1e3) / 1e9, 1) if dec_ms else None,

@@ -168,6 +168,39 @@ def test_tied_model_uses_compressed_embedding_as_head(tmp_path):
         assert torch.equal(eng.forward_logits(ids), ref)
 
 
+@pytest.mark.parametrize("vram,ram,fmt,tier", [
+    (0.0, 0.0, "decoded", "disk"), (0.1, 0.0, "decoded", "disk"),
+    (0.0, 2.0, "decoded", "ram"), (0.0, 2.0, "compressed", "ram"),
+])
+def test_tied_head_follows_streamed_embedding(tmp_path, vram, ram, fmt, tier):
+    """A tied checkpoint whose embedding the plan leaves on disk or in host
+    RAM: the head loads the same stored tensor for its own live range
+    (reference streaming_engine.py:2063-2091), so logits and greedy tokens
+    equal the in-memory model's."""
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, engine_headroom_bytes
+    cfg, model = _tiny(tie=True, seed=2)
+    snap, store, m = _store(tmp_path, cfg, model, "t")
+    total = sum(v["orig_bytes"] for v in m["tensors"].values() if not v.get("row_gather"))
+    se = 1 << 16
+    head = engine_headroom_bytes(m, EngineConfig(decode_slice_elems=se))
+    model = model.to("cuda")
+    ids = torch.randint(0, cfg.vocab_size, (1, 9), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits
+        want = ids
+        for _ in range(4):
+            want = torch.cat([want, model(input_ids=want).logits[:, -1, :].argmax(-1, keepdim=True)], 1)
+    with _engine(snap, store, decode_slice_elems=se, vram_budget_gb=(head + vram * total) / 1e9,
+                 ram_budget_gb=ram * total / 1e9, ram_tier_format=fmt, io_prefetch_depth=1) as eng:
+        assert eng.tier_of("model.embed_tokens.weight") == tier
+        got = eng.forward_logits(ids)
+        got2 = eng.forward_logits(ids)
+        seq = eng.generate_greedy(ids, 4)
+        assert eng.model.lm_head.weight.device.type == "meta"  # dropped after its use
+    assert torch.equal(got, ref) and torch.equal(got2, ref)
+    assert torch.equal(seq, want)
+
+
 def test_llama_layout_streams_bit_exact(tmp_path):
     cfg, model = _tiny(seed=3, arch="llama")
     snap, store, _ = _store(tmp_path, cfg, model, "l")
