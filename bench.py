@@ -272,7 +272,7 @@ def run_tokens(args, dev) -> dict:
             harness = torch.cuda.memory_allocated(dev)  # the harness's own buffers, not the engine's
             with StreamingLosslessModel("synthetic/%s-shape" % args.model, root / args.model, device=str(dev),
                                         config=ecfg, hf_config=cfg) as eng:
-                eng.generate_greedy(prompt, 1)  # warm: kernels, tables, allocator
+                eng.generate_greedy(prompt, 2)  # warm: prompt pass and one single-token step
                 eng.stats.reset()
                 torch.cuda.synchronize()
                 t0 = time.perf_counter()
@@ -431,7 +431,9 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
             dec = load_tp_decoder(store, cfg, world, rank, None, dev, resident=resident, **kw)
             torch.cuda.synchronize()
             load_s = _max_over_ranks(time.perf_counter() - t0, world, dev)
-            dec.generate_greedy(prompt, 1)  # warm: kernels, tables, allocator, NCCL
+            # warm: the prompt pass and one single-token step (kernels load lazily on first
+            # launch; tables, allocator, NCCL)
+            dec.generate_greedy(prompt, 2)
             torch.cuda.synchronize()
             torch.cuda.reset_peak_memory_stats(dev)
             _barrier(world)
