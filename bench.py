@@ -554,11 +554,12 @@ def run_reference(args, world, rank):
     nbytes = algorithmic_bytes(layers)
     from oracle import oracle as O
     threads = O.max_threads()
-    O.decompress(layers[1].encoded, layers[1].sign_mantissa.numpy(), threads)  # warm
-    for _ in range(args.warmup):
-        O.decompress(layers[1].encoded, layers[1].sign_mantissa.numpy(), threads)
-    # each step: one bounded sample = the q_proj-sized tensor (26 M weights)
+    # each step: one bounded sample = the workload's first tensor (q_proj, 26 M weights, for
+    # the 14B layer)
     sample = [layers[0]]
+    name, rows, cols = spec[0]
+    for _ in range(1 + args.warmup):
+        O.decompress(sample[0].encoded, sample[0].sign_mantissa.numpy(), threads)
     sb = algorithmic_bytes(sample)
     t0 = time.perf_counter()
     for _ in range(args.steps):
@@ -570,9 +571,10 @@ def run_reference(args, world, rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
             "data": "synthetic", "config": dict(bench_config(args, spec, int(nbytes), world),
-                                                sample_per_step="q_proj tensor (5120x5120)"),
+                                                sample_per_step="%s tensor (%dx%d)" % (name, rows, cols)),
             "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": "q_proj-shaped tensor per step; oracle port of the reference CPU decoder"},
+                             "sample": "%s tensor (%dx%d) per step; oracle port of the reference CPU decoder"
+                                       % (name, rows, cols)},
             "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "layer_algorithmic_bytes": nbytes}
     print(json.dumps(line), flush=True)

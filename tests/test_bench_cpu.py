@@ -1,0 +1,41 @@
+"""bench.py host logic on the CPU: the reference arm's JSON line (it times
+the oracle port of the reference's CPU decoder, so it runs without a GPU)
+and the decoder configurations the tokens/s measurements build."""
+import io
+import json
+import contextlib
+
+import pytest
+
+import bench
+
+
+def test_reference_arm_prints_the_contract_line():
+    out = io.StringIO()
+    with contextlib.redirect_stdout(out):
+        rc = bench.main(["--impl", "reference", "--steps", "1", "--warmup", "3",
+                         "--workload", "config1-4096x4096"])
+    assert rc == 0
+    line = json.loads(out.getvalue().strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["metric"] == bench.METRIC and line["unit"] == "GB/s"
+    assert line["value"] > 0 and line["higher_is_better"] is True
+    assert line["config"]["workload"] == "config1-4096x4096"
+    assert line["config"]["sample_per_step"] == "w tensor (4096x4096)"
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+
+
+@pytest.mark.parametrize("name", sorted(bench.MODELS))
+def test_model_configurations(name):
+    cfg, prompt, new, budget, label = bench.model_config(name)
+    assert prompt > 0 and new > 0 and budget > 0 and label
+    assert cfg.num_attention_heads % cfg.num_key_value_heads == 0
+    # every shape shards at TP 8: KV heads and the vocabulary split evenly
+    assert cfg.num_key_value_heads % 8 == 0 and cfg.vocab_size % 8 == 0
+    assert cfg.tie_word_embeddings == (name == "qwen3-0.6b")
+
+
+def test_tp_store_chunk_size():
+    assert bench.tp_store_chunk_size(8) == 256
+    assert bench.tp_store_chunk_size(1) == bench.tp_store_chunk_size(2) == bench.tp_store_chunk_size(4) == 1024
