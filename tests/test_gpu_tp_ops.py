@@ -3,8 +3,6 @@ PyTorch references of the same ops: transformers' BF16 rounding points for
 the norms, rotary embedding and SiLU (equal up to one BF16 ulp from fp32
 reduction order), an fp32 reference for the attention (BF16 output
 tolerance)."""
-import math
-
 import pytest
 import torch
 import torch.nn.functional as F
