@@ -116,12 +116,13 @@ def test_shard_kinds():
     assert shard_kind("model.layers.0.self_attn.q_norm.weight") == "rep"
 
 
-def _tiny(seed=0, tie=False):
-    from transformers import AutoModelForCausalLM, Qwen3Config
+def _tiny(seed=0, tie=False, arch="qwen3"):
+    from transformers import AutoModelForCausalLM, LlamaConfig, Qwen3Config
     torch.manual_seed(seed)
-    cfg = Qwen3Config(vocab_size=512, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
-                      num_attention_heads=4, num_key_value_heads=2, head_dim=32, max_position_embeddings=64,
-                      tie_word_embeddings=tie)
+    shape = dict(vocab_size=512, hidden_size=128, intermediate_size=256, num_hidden_layers=2,
+                 num_attention_heads=4, num_key_value_heads=2, head_dim=32, max_position_embeddings=64,
+                 tie_word_embeddings=tie)
+    cfg = Qwen3Config(**shape) if arch == "qwen3" else LlamaConfig(**shape)
     m = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16).eval()
     with torch.no_grad():
         for p in m.parameters():
@@ -147,11 +148,11 @@ def _shard_weights(sd, world, rank, tie):
     return w
 
 
-def _worker(rank, world, port, seed, tie, q):
+def _worker(rank, world, port, seed, tie, arch, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        cfg, m = _tiny(seed, tie)
+        cfg, m = _tiny(seed, tie, arch)
         w = _shard_weights(m.state_dict(), world, rank, tie)
         dec = TPDecoder(cfg, w, world, rank, None, "cpu")
         ids = torch.randint(0, cfg.vocab_size, (1, 9), generator=torch.Generator().manual_seed(5))
@@ -168,11 +169,12 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("world,tie", [(2, False), (2, True)])
-def test_tp_forward_matches_transformers_on_cpu(world, tie):
+@pytest.mark.parametrize("world,tie,arch", [(2, False, "qwen3"), (2, True, "qwen3"), (2, False, "llama")])
+def test_tp_forward_matches_transformers_on_cpu(world, tie, arch):
+    """Qwen3 (q/k RMSNorm) and Llama (none) layouts, tied and untied heads."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_worker, args=(r, world, PORTS[(world, tie)], 3, tie, q))
+    procs = [ctx.Process(target=_worker, args=(r, world, PORTS[(world, tie, arch)], 3, tie, arch, q))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -180,7 +182,7 @@ def test_tp_forward_matches_transformers_on_cpu(world, tie):
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    cfg, m = _tiny(3, tie)
+    cfg, m = _tiny(3, tie, arch)
     ids = torch.randint(0, cfg.vocab_size, (1, 9), generator=torch.Generator().manual_seed(5))
     with torch.no_grad():
         ref = m(input_ids=ids).logits[0].float()
@@ -203,7 +205,7 @@ def test_tp_forward_matches_transformers_on_cpu(world, tie):
             cur = seq[:, :10 + t]
 
 
-PORTS = {(2, False): _free_port(), (2, True): _free_port()}
+PORTS = {key: _free_port() for key in ((2, False, "qwen3"), (2, True, "qwen3"), (2, False, "llama"))}
 
 
 def test_adjacent_views_join_back_to_back_projections():
