@@ -19,12 +19,14 @@ def sample_categorical(p: torch.Tensor, generator: torch.Generator | None = None
 
 
 def temperature_probs(logits: torch.Tensor, temperature: float) -> torch.Tensor:
-    """softmax(logits / T), or one-hot at the argmax when T <= 0."""
+    """softmax(logits / T), or one-hot at the argmax when T <= 0, in the
+    logits' own dtype (BF16 logits give BF16 probabilities, as in the
+    reference), so a seeded generator samples the same tokens."""
     if temperature <= 0:
-        probs = torch.zeros_like(logits, dtype=torch.float32)
+        probs = torch.zeros_like(logits)
         probs.scatter_(-1, logits.argmax(dim=-1, keepdim=True), 1.0)
         return probs
-    return torch.softmax(logits.float() / temperature, dim=-1)
+    return torch.softmax(logits / temperature, dim=-1)
 
 
 def speculative_sample_step(draft_probs: list[torch.Tensor], target_probs: list[torch.Tensor],
