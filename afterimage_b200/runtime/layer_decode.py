@@ -75,10 +75,6 @@ class ResidentLayer:
     def n(self) -> int:
         return int(self.encoded.n_symbols)
 
-    def device_bytes(self) -> int:
-        return (self.stream.capacity + self.stream.offsets.numel() * 8 + self.sign_mantissa.numel()
-                + self.tables.block.numel() + self.tables.sym_lut.numel() * 4 + self.tables.len_lut.numel())
-
 
 def upload_layer(layer: CompressedLayer, device) -> ResidentLayer:
     """Host -> device copy of one compressed tensor plus its decode tables
