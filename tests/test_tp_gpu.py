@@ -72,6 +72,41 @@ def test_tp_single_gpu_matches_transformers(stores, resident, kw, which):
         dec.close()
 
 
+@pytest.fixture(scope="module")
+def tied_store(tmp_path_factory):
+    from afterimage_b200.runtime.streaming_engine import write_store
+    tmp = tmp_path_factory.mktemp("tp_tied")
+    cfg, model = _tiny(tie=True, seed=22, layers=2)
+    items = ((k, v.contiguous()) for k, v in model.state_dict().items() if k != "lm_head.weight")
+    write_store(items, tmp / "tied", tied=True, tp_row_chunks=4)
+    return cfg, model, tmp / "tied"
+
+
+@pytest.mark.parametrize("resident,kw", [("decoded", {}), ("compressed", {}), ("streamed", {}),
+                                         ("streamed", {"vram_budget_gb": 100.0})])
+def test_tp_tied_head_matches_transformers(tied_store, resident, kw):
+    """A tied checkpoint (no lm_head.weight in the store): the head is this
+    rank's vocabulary rows of the embedding, in every residency mode, eager
+    and graphed."""
+    from afterimage_b200.runtime.tp_decoder import load_tp_decoder
+    cfg, model, store = tied_store
+    dec = load_tp_decoder(store, cfg, 1, 0, None, "cuda", resident=resident, **kw)
+    model = model.to("cuda")
+    ids = torch.randint(0, cfg.vocab_size, (1, 10), device="cuda",
+                        generator=torch.Generator(device="cuda").manual_seed(8))
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits[0].float()
+    got = dec.forward(ids).float()
+    assert torch.allclose(got, ref, atol=2e-2, rtol=0), float((got - ref).abs().max())
+    ref_seq, margins = _ref_greedy(model, ids, 5)
+    _check_greedy(dec.generate_greedy(ids, 5), ref_seq, margins, 10)
+    if resident != "streamed":
+        _check_greedy(dec.generate_greedy_graphed(ids, 5), ref_seq, margins, 10)
+    if resident != "decoded":
+        _lib_status_clear()
+    dec.close()
+
+
 @pytest.mark.parametrize("resident,kw", [("decoded", {}), ("compressed", {}), ("compressed", {"overlap": True}),
                                          ("decoded", {"fused": False}), ("compressed", {"fused": False})])
 def test_tp_graphed_generation(stores, resident, kw):
