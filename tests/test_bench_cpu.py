@@ -39,3 +39,12 @@ def test_model_configurations(name):
 def test_tp_store_chunk_size():
     assert bench.tp_store_chunk_size(8) == 256
     assert bench.tp_store_chunk_size(1) == bench.tp_store_chunk_size(2) == bench.tp_store_chunk_size(4) == 1024
+
+
+def test_cpu_baseline_reports_all_threads_and_one_thread():
+    spec = bench.WORKLOADS["config1-4096x4096"]
+    layers = bench.make_layers(spec, 3, "cpu", bench.WORKLOAD_CHUNKS.get("config1-4096x4096"))
+    cpu = bench.cpu_baseline(layers, max_seconds=0.5)
+    assert cpu["kind"] == "port" and cpu["value"] > 0 and cpu["cores"] >= 1
+    one = cpu["single_thread"]
+    assert one["cores"] == 1 and one["value"] > 0 and one["sample"].endswith("4096x4096 tensor")
