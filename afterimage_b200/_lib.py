@@ -29,6 +29,7 @@ STATUS_BAD_CHUNK_RANGE = 1
 STATUS_LUT_NOT_PREFIX = 2
 STATUS_LUT_RANGE = 4
 STATUS_WAIT_TIMEOUT = 8
+WAIT_LIMIT_POLLS = 1 << 22  # AIB_WAIT_LIMIT_POLLS
 
 P = ctypes.c_void_p
 I64 = ctypes.c_int64
@@ -93,6 +94,7 @@ SIGNATURES = [
     ("aib_decode_gemv_bf16_batch", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
     ("aib_decode_gemv_bf16_batch_noalloc", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
     ("aib_recombine", CI, [P, P, I64, P, P]),
+    ("aib_selftest_wait_timeout", CI, [ctypes.c_uint, P, P]),
     ("aib_add_rmsnorm_bf16", CI, [P, P, P, P, I64, I64, ctypes.c_float, P]),
     ("aib_qk_rope_cache_bf16", CI, [P, CI, CI, CI, CI, P, P, ctypes.c_float, P, P, P, P, P, I64, P]),
     ("aib_decode_attention_bf16", CI, [P, P, P, CI, CI, CI, I64, P, ctypes.c_float, P, P]),

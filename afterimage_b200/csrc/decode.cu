@@ -104,7 +104,7 @@ constexpr int kSlots = AIB_SLOTS;                // stream ring slots per lane (
 constexpr int kSlotRow = kSlots * 16 + 16;       // padded: lanes' slot k spread over the banks
 constexpr int kStreamWarpBytes = 32 * kSlotRow;
 constexpr int kSmemBytes = kFastBytes + kWarps * (kRingWarpBytes + kStreamWarpBytes);
-constexpr unsigned kWaitLimit = 1u << 22;  // bounded mbarrier wait (~0.3 s with backoff)
+constexpr unsigned kWaitLimit = AIB_WAIT_LIMIT_POLLS;  // bounded mbarrier wait (polls, with backoff)
 
 enum Mode { kModeBF16 = 0, kModeU8 = 1, kModeI32 = 2 };
 constexpr int kDefaultChunk = 1024;  // compress_layer's default chunk_size
@@ -582,6 +582,22 @@ __device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast,
 // table's flags say the reference LUT is not a plain prefix-code table
 // (every lookup then takes the exact slow path). Returns false, uniformly
 // for the CTA, when the copy did not complete in time.
+// Polls `bar` for the phase of `parity` at most `limit` times, with backoff.
+// Every thread of the CTA gets the same answer: true when the wait gave up.
+__device__ __forceinline__ bool cta_wait_gave_up(uint64_t *bar, unsigned parity, unsigned limit) {
+  unsigned spins = 0;
+  int timed_out = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (++spins > limit) {
+      timed_out = 1;
+      break;
+    }
+    __nanosleep(64);
+  }
+  // the whole CTA leaves together so no barrier below misses a thread
+  return __syncthreads_or(timed_out) != 0;
+}
+
 __device__ __forceinline__ bool stage_table(uint2 *s_fast, const uint2 *src, const int32_t *flags, uint64_t *bar,
                                             int32_t *status) {
   if (threadIdx.x == 0) {
@@ -590,17 +606,7 @@ __device__ __forceinline__ bool stage_table(uint2 *s_fast, const uint2 *src, con
     bulk_g2s(s_fast, src, kFastBytes, bar);
   }
   __syncthreads();
-  unsigned spins = 0;
-  int timed_out = 0;
-  while (!mbar_try_wait(bar, 0)) {
-    if (++spins > kWaitLimit) {
-      timed_out = 1;
-      break;
-    }
-    __nanosleep(64);
-  }
-  // the whole CTA leaves together so no barrier below misses a thread
-  if (__syncthreads_or(timed_out)) {
+  if (cta_wait_gave_up(bar, 0, kWaitLimit)) {
     if (status && threadIdx.x == 0) atomicOr(status, AIB_STATUS_WAIT_TIMEOUT);
     return false;
   }
@@ -838,6 +844,16 @@ __global__ void recombine_kernel(const uint8_t *__restrict__ e, const uint8_t *_
   } else {
     for (int64_t t = i; t < n; t += stride) out[t] = combine1(e[t], sm[t]);
   }
+}
+
+// Self-test of the bounded wait: one CTA waits on an mbarrier whose phase
+// nothing completes (no copy is issued, nobody arrives), gives up after
+// `limit` polls and reports it the way a stalled table copy does.
+__global__ void wait_timeout_selftest_kernel(unsigned limit, int32_t *status) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) mbar_init(&bar, 1);
+  __syncthreads();
+  if (cta_wait_gave_up(&bar, 0, limit) && threadIdx.x == 0) atomicOr(status, AIB_STATUS_WAIT_TIMEOUT);
 }
 
 // ---------------------------------------------------------------------------
@@ -1252,6 +1268,16 @@ AIB_API int aib_decode_gemv_bf16_batch_noalloc(const aib_gemv_desc *descs, int c
   if (off > AIB_GEMV_SCRATCH_FLOATS)
     return aib_set_error("gemv: the batch's aligned scratch areas do not fit"), AIB_EINVAL;
   return gemv_launch(local, count, d_status, stream);
+}
+
+AIB_API int aib_selftest_wait_timeout(unsigned polls, int32_t *d_status, void *stream) {
+  if (!d_status) return aib_set_error("aib_selftest_wait_timeout: null status"), AIB_EINVAL;
+  if (polls < 1 || polls > kWaitLimit)
+    return aib_set_errorf("aib_selftest_wait_timeout: polls must be in [1, %u], got %u", kWaitLimit, polls),
+           AIB_EINVAL;
+  wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(polls, d_status);
+  AIB_CUDA(cudaGetLastError());
+  return AIB_OK;
 }
 
 AIB_API int aib_recombine(const uint8_t *exponent, const uint8_t *sign_mantissa, int64_t n, uint16_t *out,

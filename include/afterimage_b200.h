@@ -38,6 +38,11 @@ extern "C" {
 #define AIB_STATUS_LUT_RANGE 4       /* tables: a symbol outside [0, 255] or a length outside [0, max_bits] */
 #define AIB_STATUS_WAIT_TIMEOUT 8    /* a bounded wait on a bulk copy gave up; the CTA returned early */
 
+/* Polls of the kernels' one device-side wait (the table's bulk copy, with a
+ * short sleep between polls) before the CTA gives up with
+ * AIB_STATUS_WAIT_TIMEOUT. */
+#define AIB_WAIT_LIMIT_POLLS (1u << 22)
+
 /* Thread-local message for the last failing call on this thread. */
 const char *aib_last_error(void);
 /* ABI version: bump on any signature change. */
@@ -227,6 +232,14 @@ int aib_silu_mul_bf16(const void *gate_up, void *out, int64_t T, int64_t I, void
  * (afterimage/runtime/compressed_store.py:94-130). */
 int aib_recombine(const uint8_t *exponent, const uint8_t *sign_mantissa, int64_t n, uint16_t *out,
                   void *stream);
+
+/* Self-test of the bounded device wait; it has no counterpart in the
+ * reference. One CTA waits on an mbarrier that nothing completes, gives up
+ * after `polls` polls (1..AIB_WAIT_LIMIT_POLLS) and ORs
+ * AIB_STATUS_WAIT_TIMEOUT into *d_status, as a table copy that never lands
+ * would. No copy is issued, so nothing outlives the CTA. Enqueued on
+ * `stream`; no synchronisation. */
+int aib_selftest_wait_timeout(unsigned polls, int32_t *d_status, void *stream);
 
 #ifdef __cplusplus
 }

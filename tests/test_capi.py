@@ -175,3 +175,14 @@ def test_pread_batch_reads_pieces_in_parallel(tmp_path):
     finally:
         os.close(fd)
     assert L.aib_pread_batch(-1, None, None, None, None, 0, 1, None) == _lib.AIB_EINVAL
+
+
+def test_wait_timeout_selftest_validates_on_the_host():
+    L = _lib.load()
+    m = re.search(r"#define AIB_WAIT_LIMIT_POLLS \(1u << (\d+)\)", HEADER.read_text())
+    assert m and _lib.WAIT_LIMIT_POLLS == 1 << int(m.group(1))
+    status = ctypes.c_void_p(16)  # never dereferenced: each call fails validation first
+    assert L.aib_selftest_wait_timeout(0, status, None) == _lib.AIB_EINVAL
+    assert L.aib_selftest_wait_timeout(_lib.WAIT_LIMIT_POLLS + 1, status, None) == _lib.AIB_EINVAL
+    assert L.aib_selftest_wait_timeout(1, None, None) == _lib.AIB_EINVAL
+    assert b"polls" in L.aib_last_error() or b"null" in L.aib_last_error()
