@@ -21,6 +21,13 @@ decode has no exchange step), so scaling is weak and the data path has no
 collective. `--impl reference` times the reference's CPU decode path (the
 oracle port of its numba decoder + recombine, all host threads) on the same
 workload and metric.
+
+The same line carries the tokens/s half of the metric: greedy decoding of a
+random-init decoder of the `--model` shape (Qwen3-0.6B, Llama-3-8B,
+Qwen3-14B by default, or Mistral-Small-24B) through the tensor-parallel
+decoder at the run's N (streamed from host memory, streamed under the
+configuration's per-rank VRAM budget, compressed-resident eager and
+graphed), and with `--tokens` through the transformers-driven engine.
 """
 from __future__ import annotations
 
@@ -51,7 +58,7 @@ WORKLOADS = {"qwen3-14b-layer": QWEN3_14B_LAYER, "config1-4096x4096": CONFIG1,
 # whole chunks of every rank's columns)
 WORKLOAD_CHUNKS = {"qwen3-14b-layer-tp8": {"o_proj": 640, "down_proj": 1088}}
 FAST_TABLE_BYTES = 4096 * 8
-# the benchmark's Qwen3-0.6B- and Qwen3-14B-shaped decoder configurations, random-init weights
+# the benchmark's decoder shapes (random-init weights in every measurement)
 QWEN3_06B = dict(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
                  num_attention_heads=16, num_key_value_heads=8, head_dim=128, rope_theta=1e6,
                  tie_word_embeddings=True, max_position_embeddings=4096)
@@ -405,6 +412,8 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
       streamed:            compressed shards in page-locked host memory,
                            copied to the GPU one layer at a time (the layer
                            streamer over PCIe; device memory stays a few GB);
+      streamed_<B>GB_per_rank: the same under the configuration's per-rank
+                           VRAM budget (the planner keeps what fits resident);
       compressed_resident: compressed shards resident in HBM, decoded per
                            layer per forward, the next layer's decode
                            overlapping this layer's projections.
