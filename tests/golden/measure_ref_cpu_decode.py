@@ -12,7 +12,7 @@ reference's own CPU speed.
 
 Usage (in a container that has an Afterimage checkout):
 
-    python oracle/compare_ref_cpu_decode.py <path to the checkout> [--rows 5120 --cols 5120]
+    python tests/golden/measure_ref_cpu_decode.py <path to the checkout> [--rows 5120 --cols 5120]
 
 Prints one line per thread count: best of 3 for each, the ratio, and
 whether the outputs are equal.
@@ -33,7 +33,7 @@ sys.dont_write_bytecode = True
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REPO = pathlib.Path(__file__).resolve().parent.parent
+REPO = pathlib.Path(__file__).resolve().parents[2]
 
 
 def best_of(fn, n: int = 3) -> float:

@@ -12,7 +12,7 @@ forced greedy tokens are the configuration's count.
 
 Usage (in a container that has an Afterimage checkout):
 
-    python oracle/ref_engine_tokens_cpu.py <path to the checkout> [--model qwen3-0.6b]
+    python tests/golden/measure_ref_engine_tokens_cpu.py <path to the checkout> [--model qwen3-0.6b]
 
 Prints one JSON line: tokens/s, s/token, torch threads, compression time.
 The reference is imported read-only (no bytecode written, numba cache in a
@@ -35,7 +35,7 @@ sys.dont_write_bytecode = True
 
 import torch  # noqa: E402
 
-REPO = pathlib.Path(__file__).resolve().parent.parent
+REPO = pathlib.Path(__file__).resolve().parents[2]
 
 
 def main() -> None:
