@@ -43,7 +43,8 @@ extern "C" {
  * AIB_STATUS_WAIT_TIMEOUT. */
 #define AIB_WAIT_LIMIT_POLLS (1u << 22)
 
-/* Thread-local message for the last failing call on this thread. */
+/* Thread-local message for the last failing call on this thread (the
+ * library's error channel; no counterpart in the reference). */
 const char *aib_last_error(void);
 /* ABI version: bump on any signature change. */
 int aib_abi_version(void);
@@ -74,14 +75,17 @@ int aib_pack_chunks(const uint8_t *symbols, int64_t n, int64_t chunk_size,
                     const int32_t lengths[256], const uint32_t codes[256],
                     const int32_t *chunk_nbytes, int32_t *chunk_offsets, uint8_t *out,
                     int64_t out_capacity);
-/* Host threads the encoder uses (OpenMP). */
+/* Host threads the encoder uses (OpenMP); a utility with no counterpart in
+ * the reference. */
 int aib_host_threads(void);
 
 /* ------------------------------------------------------------------------
  * Store reads -- the extents of BinaryWeightReader.read_many
  * (afterimage/runtime/binstore.py:109-192)
  * ------------------------------------------------------------------------ */
-/* n positional reads of file descriptor fd: piece i fills dests[i] with
+/* Replaces the extent reads of BinaryWeightReader.read_many
+ * (afterimage/runtime/binstore.py:109-192).
+ * n positional reads of file descriptor fd: piece i fills dests[i] with
  * sizes[i] bytes from offsets[i]. `threads` host threads read pieces
  * concurrently; *bytes_read receives the bytes read. If min_sizes is not
  * NULL, a piece that reaches end of file after min_sizes[i] bytes is
@@ -175,7 +179,10 @@ typedef struct aib_gemv_desc {
   void *y;            /* device bf16[(elem_end - elem_begin) / cols] */
 } aib_gemv_desc;
 
-/* Up to AIB_MAX_BATCH GEMVs (each with its own x) in one launch pair: the
+/* Replaces, for one token, a layer's decode followed by the nn.Linear /
+ * F.linear that consumes it (afterimage/runtime/streaming_engine.py:1871-1915,
+ * :2330): y = W x with W read only in compressed form.
+ * Up to AIB_MAX_BATCH GEMVs (each with its own x) in one launch pair: the
  * decode-and-multiply kernel writes one fp32 partial per chunk, a second
  * kernel sums each row's partials in column order and rounds to BF16
  * (deterministic). Work is enqueued on `stream`; no synchronisation. */
