@@ -181,17 +181,21 @@ class BinaryWeightReader:
         return self._fh.readinto(view)
 
     def read_many(self, refs: list[dict], *, max_gap_bytes: int = 0, max_extent_bytes: int = 1 << 28,
-                  verify: bool = False, pinned: PinnedBuffer | bool = False
+                  verify: bool = False, pinned: PinnedBuffer | bool = False, groups: list | None = None
                   ) -> tuple[list[np.ndarray], int, int]:
         """Reads blobs through bounded contiguous extents (reference
         binstore.py:109-192). Returns (arrays in the caller's order, number
         of read calls, bytes read). With `pinned`, every extent lands in one
         page-locked buffer (a PinnedBuffer to reuse, or True for a fresh
-        one); the arrays view that buffer and stay valid until it is reused."""
+        one); the arrays view that buffer and stay valid until it is reused.
+        With `groups` (one label per ref), blobs merge only with neighbours
+        of the same label: per-tensor extents in one call."""
         if max_gap_bytes < 0:
             raise ValueError("max_gap_bytes must be non-negative")
         if max_extent_bytes < 1:
             raise ValueError("max_extent_bytes must be positive")
+        if groups is not None and len(groups) != len(refs):
+            raise ValueError("groups needs one label per ref")
         if not refs:
             return [], 0, 0
         ordered = sorted(enumerate(refs), key=lambda item: int(item[1]["offset"]))
@@ -205,7 +209,8 @@ class BinaryWeightReader:
                 prev = extents[-1]
                 gap = start - prev["end"]
                 merged_end = max(prev["end"], end)
-                if 0 <= gap <= max_gap_bytes and merged_end - prev["start"] <= max_extent_bytes:
+                same = groups is None or groups[idx] == groups[prev["items"][-1][0]]
+                if same and 0 <= gap <= max_gap_bytes and merged_end - prev["start"] <= max_extent_bytes:
                     prev["end"] = merged_end
                     prev["items"].append((idx, ref))
                     continue

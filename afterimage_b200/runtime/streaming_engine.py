@@ -31,6 +31,7 @@ import concurrent.futures
 import dataclasses
 import json
 import pathlib
+import sys
 import threading
 import time
 
@@ -73,6 +74,14 @@ class EngineConfig:
     spec_k: int = 8
     lm_head_slice_rows: int = 0             # reference config: rows of lm_head per block, 0 = whole
     max_inflight_layers: int = 2            # streamed layers whose device buffers may be alive at once
+    # further reference fields on this path (config.py:362-406)
+    block_chunks: int = 32                  # validated like the reference; the CUDA grouping is fixed at 32
+    vram_safety_margin_gb: float = 0.0      # extra non-residency reserve inside vram_budget_gb
+    storage_read_policy: str = "coalesced_extents"  # "per_blob" | "coalesced_extents" | "tensor_extents"
+    empty_cache_every: int = 0              # release cached device blocks every N layer frees; 0 never
+    progress: bool = False                  # print generation progress to stderr
+    require_pinned_ram: bool = False        # a failed pin of the decoded RAM tier always raises here
+    placement_policy: str = "traffic_density"  # the planner's ranking; profiled ones are out of scope
 
     def __post_init__(self):
         if self.chunk_size < 1:
@@ -95,6 +104,35 @@ class EngineConfig:
             raise ValueError("vram_tier_format must be 'decoded' or 'compressed'")
         if self.ram_budget_gb is not None and self.vram_budget_gb is None:
             raise ValueError("ram_budget_gb requires vram_budget_gb (the planner decides both tiers)")
+        if self.block_chunks & (self.block_chunks - 1) != 0:
+            raise ValueError("block_chunks must be a power of 2, got %d" % self.block_chunks)
+        if self.storage_read_policy not in ("per_blob", "coalesced_extents", "tensor_extents"):
+            raise ValueError("storage_read_policy must be 'per_blob', 'coalesced_extents' or 'tensor_extents', "
+                             "got %r" % (self.storage_read_policy,))
+        if self.storage_extent_max_bytes < 1:
+            raise ValueError("storage_extent_max_bytes must be positive")
+        if self.storage_extent_max_gap_bytes < 0:
+            raise ValueError("storage_extent_max_gap_bytes must be non-negative")
+        if self.max_context is not None and self.max_context < 1:
+            raise ValueError("max_context must be >= 1, got %d" % self.max_context)
+        if self.max_context is not None and self.vram_budget_gb is None:
+            raise ValueError("max_context requires vram_budget_gb (the KV reserve is part of the plan)")
+        if self.vram_safety_margin_gb < 0:
+            raise ValueError("vram_safety_margin_gb must be non-negative")
+        if self.vram_safety_margin_gb and self.vram_budget_gb is None:
+            raise ValueError("vram_safety_margin_gb requires vram_budget_gb")
+        if self.empty_cache_every < 0:
+            raise ValueError("empty_cache_every must be >= 0")
+        if self.require_pinned_ram and self.ram_budget_gb is None:
+            raise ValueError("require_pinned_ram requires ram_budget_gb")
+        if self.require_pinned_ram and self.ram_tier_format != "decoded":
+            raise ValueError("require_pinned_ram requires ram_tier_format='decoded'")
+        if self.placement_policy not in ("traffic_density", "profiled_knapsack", "critical_path",
+                                         "replay_cem", "replay_qubo", "replay_extent_qubo"):
+            raise ValueError("unknown placement_policy %r" % (self.placement_policy,))
+        if self.placement_policy != "traffic_density":
+            raise ValueError("placement_policy=%r needs measured critical-path profiles or replay plans; "
+                             "this package does not build them (only 'traffic_density')" % self.placement_policy)
 
     @property
     def uses_tiered_residency(self) -> bool:
@@ -442,6 +480,7 @@ class StreamingLosslessModel:
         self._futures: dict[int, concurrent.futures.Future] = {}
         self._inflight: list = []   # (layer, compute-stream event after its forward), oldest first
         self._head_future = None
+        self._frees = 0             # layer frees, for empty_cache_every
         self._head_reader = None
         self._head_buf = None
         if self._chunked_head_rows():
@@ -525,10 +564,11 @@ class StreamingLosslessModel:
         if cfg.max_context is not None:
             slack += kv_cache_bytes_per_token(self.hf_cfg) * cfg.max_context
         stream_only = self._stream_only_overrides()
-        headroom = engine_headroom_bytes(self.manifest, cfg, stream_only, slack)
+        headroom = (engine_headroom_bytes(self.manifest, cfg, stream_only, slack)
+                    + int(cfg.vram_safety_margin_gb * 1e9))
         plan = plan_from_manifest(self.manifest, vram_budget_gb=cfg.vram_budget_gb,
                                   ram_budget_gb=cfg.ram_budget_gb or 0.0, stream_only=stream_only,
-                                  vram_headroom_bytes=headroom)
+                                  vram_headroom_bytes=headroom, placement_policy=cfg.placement_policy)
         if not plan.feasible:
             raise RuntimeError("VRAM budget is infeasible: " + plan.reason)
         self.plan = plan
@@ -544,12 +584,21 @@ class StreamingLosslessModel:
         return self._tier.get(key, "disk")
 
     def _read_arrays(self, keys: list[str], reader: BinaryWeightReader, pinned) -> dict[str, dict]:
+        """Every blob of `keys` in one read_many call, merged into extents as
+        storage_read_policy says: "per_blob" one read per stored array,
+        "tensor_extents" adjacent arrays of one tensor, "coalesced_extents"
+        adjacent arrays of all of them (within the gap / extent bounds). The
+        policy changes the reads, never the bytes."""
+        cfg = self.config
         named = [(k, name, ref) for k in keys for name, ref in self.manifest["tensors"][k]["blobs"].items()]
+        per_blob = cfg.storage_read_policy == "per_blob"
         t0 = time.perf_counter()
         arrays, calls, nbytes = reader.read_many([r for _, _, r in named],
-                                                 max_gap_bytes=self.config.storage_extent_max_gap_bytes,
-                                                 max_extent_bytes=self.config.storage_extent_max_bytes,
-                                                 pinned=pinned)
+                                                 max_gap_bytes=0 if per_blob else cfg.storage_extent_max_gap_bytes,
+                                                 max_extent_bytes=1 if per_blob else cfg.storage_extent_max_bytes,
+                                                 pinned=pinned,
+                                                 groups=[k for k, _, _ in named]
+                                                 if cfg.storage_read_policy == "tensor_extents" else None)
         out: dict[str, dict] = {k: {} for k in keys}
         for (k, name, _), a in zip(named, arrays):
             out[k][name] = a
@@ -765,6 +814,10 @@ class StreamingLosslessModel:
             if self.tier_of(k) == "vram" and k not in self._vram_compressed:
                 continue
             _to_meta(self.model, k)
+        self._frees += 1
+        every = self.config.empty_cache_every
+        if every and self._frees % every == 0:
+            torch.cuda.empty_cache()
 
     def _install_hooks(self) -> None:
         """transformers drives the stack (masks, rotary, cache); hooks only
@@ -901,17 +954,32 @@ class StreamingLosslessModel:
         seq = input_ids.to(self.device)
         self._kv_cache = None
         step = seq
-        for _ in range(max_new_tokens):
+        t0 = time.perf_counter()
+        for i in range(max_new_tokens):
             logits = self.forward_logits(step, use_cache=use_cache)
             nxt = logits[:, -1, :].argmax(dim=-1, keepdim=True)
             seq = torch.cat([seq, nxt], dim=1)
             step = nxt if use_cache else seq
             tok = int(nxt.item())
+            self._progress(i + 1, max_new_tokens, t0)
             if on_token is not None:
                 on_token(tok)
             if tok in stop_token_ids:
                 break
+        self._progress(None, max_new_tokens, t0)
         return seq
+
+    def _progress(self, done: int | None, total: int, t0: float) -> None:
+        """One stderr line per generated token when config.progress is set
+        (done=None ends the line)."""
+        if not self.config.progress:
+            return
+        if done is None:
+            sys.stderr.write("\n")
+        else:
+            dt = time.perf_counter() - t0
+            sys.stderr.write("\r[afterimage_b200] token %d/%d, %.2f s/token" % (done, total, dt / done))
+        sys.stderr.flush()
 
     @torch.no_grad()
     def generate_speculative(self, input_ids: torch.Tensor, max_new_tokens: int, draft_model, k: int | None = None,

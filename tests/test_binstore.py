@@ -79,6 +79,26 @@ def test_read_many_respects_extent_bound_and_original_order(tmp_path):
     assert calls == 3 and nbytes == 96 and [int(a[0]) for a in got] == [2, 0, 1]
 
 
+@pytest.mark.parametrize("pinned", [False, True])
+def test_read_many_groups_merge_only_within_a_label(tmp_path, pinned):
+    """Per-tensor extents in one call: adjacent blobs of different labels
+    stay separate reads; the arrays are the same either way."""
+    arrays = [np.full(40, v, dtype=np.uint8) for v in range(6)]
+    refs = _store(tmp_path / "w.bin", arrays)
+    order = [4, 0, 5, 2, 1, 3]
+    labels = ["a", "a", "b", "b", "c", "c"]
+    with BinaryWeightReader(tmp_path / "w.bin", threads=2) as r:
+        merged, calls_all, _ = r.read_many([refs[i] for i in order], pinned=pinned)
+        merged = [a.copy() for a in merged]
+        grouped, calls_grp, nbytes = r.read_many([refs[i] for i in order], pinned=pinned,
+                                                 groups=[labels[i] for i in order])
+    assert calls_all == 1 and calls_grp == 3 and nbytes == 240
+    assert all(np.array_equal(a, b) for a, b in zip(merged, grouped))
+    assert [int(a[0]) for a in grouped] == order
+    with BinaryWeightReader(tmp_path / "w.bin") as r, pytest.raises(ValueError, match="one label per ref"):
+        r.read_many(refs, groups=["a"])
+
+
 def test_read_many_unaligned_views_are_writable_and_torch_consumable(tmp_path):
     arrays = [np.arange(7, dtype=np.uint8), np.arange(5, dtype=np.uint32), np.arange(3, dtype=np.float32),
               np.arange(9, dtype=np.uint16).reshape(3, 3)]

@@ -77,8 +77,40 @@ def test_engine_rejects_bad_schema_and_truncated_store_before_any_device_use(unt
 
 
 def test_engine_config_validation():
+    """The reference's rules (config.py:412-511) for the fields this engine
+    keeps, including the decode and read knobs that change no values."""
     from afterimage_b200.runtime.streaming_engine import EngineConfig
     for bad in (dict(chunk_size=0), dict(max_bits=17), dict(io_prefetch_depth=-1),
-                dict(ram_tier_format="x"), dict(vram_tier_format="y"), dict(ram_budget_gb=1.0)):
+                dict(ram_tier_format="x"), dict(vram_tier_format="y"), dict(ram_budget_gb=1.0),
+                dict(block_chunks=24), dict(storage_read_policy="x"), dict(storage_extent_max_bytes=0),
+                dict(storage_extent_max_gap_bytes=-1), dict(max_context=16), dict(max_context=0, vram_budget_gb=1.0),
+                dict(vram_safety_margin_gb=0.5), dict(vram_safety_margin_gb=-1.0, vram_budget_gb=1.0),
+                dict(empty_cache_every=-1), dict(require_pinned_ram=True),
+                dict(require_pinned_ram=True, vram_budget_gb=1.0, ram_budget_gb=1.0, ram_tier_format="compressed"),
+                dict(placement_policy="nope"), dict(placement_policy="critical_path", vram_budget_gb=1.0)):
         with pytest.raises(ValueError):
             EngineConfig(**bad)
+    EngineConfig(block_chunks=128, storage_read_policy="tensor_extents", vram_budget_gb=2.0,
+                 vram_safety_margin_gb=0.25, max_context=512, empty_cache_every=8, progress=True,
+                 ram_budget_gb=1.0, require_pinned_ram=True)
+
+
+@pytest.mark.parametrize("policy", ["per_blob", "tensor_extents", "coalesced_extents"])
+def test_read_policies_change_reads_not_bytes(untied_store, policy):
+    """storage_read_policy: one read per stored array, per tensor, or per
+    group of adjacent tensors -- the arrays are the same every time."""
+    import types
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, StreamingLosslessModel, StreamStats
+    cfg, model, snap, store, m = untied_store
+    keys = [k for k in m["tensors"] if k.startswith("model.layers.0.")]  # one layer: contiguous in the file
+    blobs = sum(len(m["tensors"][k]["blobs"]) for k in keys)
+    eng = types.SimpleNamespace(manifest=m, config=EngineConfig(storage_read_policy=policy), stats=StreamStats())
+    ref = types.SimpleNamespace(manifest=m, config=EngineConfig(storage_read_policy="per_blob"), stats=StreamStats())
+    with BinaryWeightReader(store / "weights.bin") as r:
+        got = StreamingLosslessModel._read_arrays(eng, keys, r, False)
+        want = StreamingLosslessModel._read_arrays(ref, keys, r, False)
+    calls = eng.stats.storage_read_calls
+    assert calls == {"per_blob": blobs, "tensor_extents": len(keys), "coalesced_extents": 1}[policy]
+    for k in keys:
+        for name in want[k]:
+            assert np.array_equal(np.asarray(got[k][name]), np.asarray(want[k][name])), (k, name)
