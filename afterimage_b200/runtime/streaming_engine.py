@@ -244,7 +244,7 @@ def tp_chunk_size(in_features: int, parts: int, chunk_size: int) -> int:
 
 def write_store(items, out_dir, config: EngineConfig | None = None, *, tied: bool, model_id: str = "",
                 revision: str | None = None, progress_every: int = 50, total: int | None = None,
-                tp_row_chunks: int | None = None) -> dict:
+                tp_row_chunks: int | None = None, control=None) -> dict:
     """Writes a compressed store from an iterable of (key, tensor) pairs:
     `weights.bin` + schema-v2 `manifest.json` (reference
     streaming_engine.py:345-427). The untied embedding is stored raw and
@@ -254,7 +254,11 @@ def write_store(items, out_dir, config: EngineConfig | None = None, *, tied: boo
     projections (o_proj, down_proj) use a chunk_size that divides
     in_features / P (`tp_chunk_size`), so each of P (or any divisor of P)
     ranks owns whole chunks of every row. The format is unchanged
-    (chunk_size is per tensor)."""
+    (chunk_size is per tensor).
+
+    `control` (anything with a checkpoint() method, like the reference's
+    JobControl) is called before each tensor is written: a pause/cancel
+    boundary, as in the reference."""
     cfg = config or EngineConfig()
     out_dir = pathlib.Path(out_dir)
     out_dir.mkdir(parents=True, exist_ok=True)
@@ -265,6 +269,8 @@ def write_store(items, out_dir, config: EngineConfig | None = None, *, tied: boo
     total_orig = total_comp = 0
     with BinaryWeightWriter(out_dir / "weights.bin") as writer:
         for n, (key, W) in enumerate(items, 1):
+            if control is not None:
+                control.checkpoint()
             tcfg = cfg
             if tp_row_chunks and W.dim() == 2 and key.endswith(("o_proj.weight", "down_proj.weight")):
                 cs = tp_chunk_size(int(W.shape[1]), int(tp_row_chunks), cfg.chunk_size)
@@ -296,13 +302,19 @@ def write_store(items, out_dir, config: EngineConfig | None = None, *, tied: boo
 
 
 def compress_model_to_disk(model_id: str, out_dir, config: EngineConfig | None = None, progress_every: int = 50,
-                           source_dir=None, revision: str | None = None, hf_config=None) -> dict:
+                           max_workers: int | None = None, control=None, source_dir=None,
+                           revision: str | None = None, hf_config=None) -> dict:
     """safetensors -> one `weights.bin` + `manifest.json` (schema v2),
     readable by the reference engine and by this one (reference
-    streaming_engine.py:256-428). The encoder is multi-threaded C++, so
-    tensors are compressed in-process in checkpoint order (embedding and
-    head first, as the reference writes them)."""
+    streaming_engine.py:256-428; same parameters). The encoder is
+    multi-threaded C++, so tensors are compressed in-process in checkpoint
+    order (embedding and head first, as the reference writes them):
+    `max_workers`, the reference's process-pool size, is validated and
+    otherwise unused. `control.checkpoint()` runs before each tensor."""
     from safetensors import safe_open
+
+    if max_workers is not None and max_workers < 1:
+        raise ValueError("max_workers must be >= 1")
 
     snap = _resolve_snapshot(model_id, source_dir, revision)
     shards = _weight_shards(snap)
@@ -324,7 +336,8 @@ def compress_model_to_disk(model_id: str, out_dir, config: EngineConfig | None =
                 yield key, f.get_tensor(key)
 
     return write_store(items(), out_dir, config, tied=bool(getattr(hf_config, "tie_word_embeddings", False)),
-                       model_id=model_id, revision=revision, progress_every=progress_every, total=len(tasks))
+                       model_id=model_id, revision=revision, progress_every=progress_every, total=len(tasks),
+                       control=control)
 
 
 # ---------------------------------------------------------------------------
@@ -434,10 +447,11 @@ class StreamingLosslessModel:
     CHUNKED_HEAD_KEY = "lm_head.weight"
 
     def __init__(self, model_id: str, store_dir, device: str = "cuda", config: EngineConfig | None = None,
-                 source_dir=None, hf_config=None):
+                 control=None, source_dir=None, hf_config=None):
         from transformers import AutoConfig, AutoModelForCausalLM
 
         self.config = config or EngineConfig()
+        self.control = control      # pause/cancel boundary once per layer load (checkpoint()), as the reference
         self.store = pathlib.Path(store_dir)
         self.manifest = json.loads((self.store / "manifest.json").read_text())
         self._check_store_integrity()
@@ -764,6 +778,8 @@ class StreamingLosslessModel:
         return any(self.tier_of(k) in ("disk", "ram") for k in self._layer_keys[idx])
 
     def _load_layer(self, idx: int) -> None:
+        if self.control is not None:
+            self.control.checkpoint()
         if self._streams(idx):
             self._bound_inflight(self.config.max_inflight_layers - 1)
         compute = torch.cuda.current_stream(self.device)
@@ -1021,6 +1037,18 @@ class StreamingLosslessModel:
         return seq[:, :input_ids.shape[1] + max_new_tokens]
 
     # -- lifetime ---------------------------------------------------------------
+    def quiesce_prefetch(self) -> None:
+        """Waits for every background read this engine started and drops its
+        result (reference streaming_engine.py:647-666): afterwards no reader
+        touches the store until the next forward, e.g. before a caller drops
+        the OS page cache. The next forward reads what it needs again."""
+        pending = list(self._futures.values())
+        if self._head_future is not None:
+            pending.append(self._head_future)
+        concurrent.futures.wait(pending)
+        self._futures.clear()
+        self._head_future = None
+
     def close(self) -> None:
         for fut in self._futures.values():
             fut.cancel()
@@ -1034,3 +1062,14 @@ class StreamingLosslessModel:
 
     def __exit__(self, *exc):
         self.close()
+
+
+def load_draft_model(model_id: str = "Qwen/Qwen3-0.6B", device: str = "cuda"):
+    """A small, fully resident BF16 model for generate_speculative's draft
+    step (reference streaming_engine.py:2734-2748). It must share the
+    target's vocabulary; it is loaded the ordinary way, not streamed."""
+    from transformers import AutoModelForCausalLM
+    m = AutoModelForCausalLM.from_pretrained(model_id, dtype=torch.bfloat16)
+    m.to(device)
+    m.eval()
+    return m

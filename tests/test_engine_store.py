@@ -114,3 +114,32 @@ def test_read_policies_change_reads_not_bytes(untied_store, policy):
     for k in keys:
         for name in want[k]:
             assert np.array_equal(np.asarray(got[k][name]), np.asarray(want[k][name])), (k, name)
+
+
+def test_compress_calls_control_per_tensor_and_cancels(tmp_path):
+    """compress_model_to_disk keeps the reference's parameters: `control`
+    (a pause/cancel hook with checkpoint()) runs before each tensor, and an
+    exception from it stops the write; `max_workers` is checked."""
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, compress_model_to_disk
+
+    class Control:
+        def __init__(self, cancel_at=None):
+            self.calls, self.cancel_at = 0, cancel_at
+
+        def checkpoint(self):
+            self.calls += 1
+            if self.cancel_at is not None and self.calls >= self.cancel_at:
+                raise KeyboardInterrupt("cancelled")
+
+    cfg, model = _tiny(tie=False, seed=4)
+    snap, store, m = _store(tmp_path, cfg, model, "c")
+    ctl = Control()
+    m2 = compress_model_to_disk("tiny", tmp_path / "again", EngineConfig(chunk_size=256), 0, 2, ctl, str(snap))
+    assert ctl.calls == len(m2["tensors"]) == len(m["tensors"])
+    assert (tmp_path / "again" / "weights.bin").read_bytes() == (store / "weights.bin").read_bytes()
+    with pytest.raises(KeyboardInterrupt):
+        compress_model_to_disk("tiny", tmp_path / "cancelled", EngineConfig(chunk_size=256), control=Control(3),
+                               source_dir=str(snap))
+    assert not (tmp_path / "cancelled" / "manifest.json").exists()
+    with pytest.raises(ValueError, match="max_workers"):
+        compress_model_to_disk("tiny", tmp_path / "bad", max_workers=0, source_dir=str(snap))

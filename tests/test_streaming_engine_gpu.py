@@ -62,7 +62,10 @@ def test_logits_bit_exact_vs_plain_forward(untied, depth):
         got = eng.forward_logits(ids)
         got2 = eng.forward_logits(ids)
         assert eng.stats.decode_launches > 0
-    assert torch.equal(got, ref) and torch.equal(got2, ref)
+        eng.quiesce_prefetch()  # reads started for the next forward are dropped, then redone
+        assert not eng._futures
+        got3 = eng.forward_logits(ids)
+    assert torch.equal(got, ref) and torch.equal(got2, ref) and torch.equal(got3, ref)
 
 
 @pytest.mark.parametrize("tiers", [
