@@ -24,13 +24,15 @@ from . import _device
 
 
 class DecodeTables(tuple):
-    """Tensor-local decode tables: (sym_lut, len_lut, block) on the device.
-    `block` is the library's table block (a multi-symbol first-level table
-    staged into shared memory by the kernel, plus validation flags); the
-    reference LUTs stay resident for codes longer than the first level."""
+    """Tensor-local decode tables on the device. It unpacks like the
+    reference's (sym_lut, len_lut) pair; `block` is the library's table
+    block (a multi-symbol first-level table staged into shared memory by the
+    kernel, plus validation flags). The reference LUTs stay resident for
+    codes longer than the first level."""
 
     def __new__(cls, sym_lut: torch.Tensor, len_lut: torch.Tensor, block: torch.Tensor, max_bits: int):
-        self = super().__new__(cls, (sym_lut, len_lut, block))
+        self = super().__new__(cls, (sym_lut, len_lut))
+        self.block = block
         self.max_bits = int(max_bits)
         return self
 
@@ -42,23 +44,21 @@ class DecodeTables(tuple):
     def len_lut(self) -> torch.Tensor:
         return self[1]
 
-    @property
-    def block(self) -> torch.Tensor:
-        return self[2]
+
+def _lut(x, dev, np_dtype, torch_dtype) -> torch.Tensor:
+    if isinstance(x, torch.Tensor):
+        return x.to(device=dev, dtype=torch_dtype).contiguous()
+    return _device.upload(x, dev, np_dtype)
 
 
-def prepare_decode_tables(enc, device: str = "cuda") -> DecodeTables:
-    """One tensor-local codebook; never cache across unrelated tensors
-    (reference gpu_decode_v2.py:71-76). Stream-ordered, no synchronisation."""
-    assert np.asarray(enc.sym_lut).max() <= 255, (
-        "decoder output is uint8; symbol alphabet must fit in a byte")
-    dev = _device.cuda_device(device)
-    mb = int(enc.max_bits)
+def _build(sym_lut, len_lut, max_bits: int, dev) -> DecodeTables:
+    """Device LUTs (int32 symbols, int8 lengths) plus their table block."""
+    mb = int(max_bits)
     if not 0 <= mb <= 16:
         raise ValueError(f"max_bits must be in [0, 16] for the CUDA decoder, got {mb}")
     with torch.cuda.device(dev):
-        sym = _device.upload(enc.sym_lut, dev, np.int32)
-        ln = _device.upload(enc.len_lut, dev, np.int8)
+        sym = _lut(sym_lut, dev, np.int32, torch.int32)
+        ln = _lut(len_lut, dev, np.int8, torch.int8)
         L = _lib.load()
         block = torch.empty(int(L.aib_tables_bytes()), dtype=torch.uint8, device=dev)
         _lib.check(L.aib_build_tables(sym.data_ptr(), ln.data_ptr(), mb, block.data_ptr(),
@@ -66,10 +66,23 @@ def prepare_decode_tables(enc, device: str = "cuda") -> DecodeTables:
     return DecodeTables(sym, ln, block, mb)
 
 
+def prepare_decode_tables(enc, device: str = "cuda") -> DecodeTables:
+    """One tensor-local codebook; never cache across unrelated tensors
+    (reference gpu_decode_v2.py:71-76). Stream-ordered, no synchronisation."""
+    assert np.asarray(enc.sym_lut).max() <= 255, (
+        "decoder output is uint8; symbol alphabet must fit in a byte")
+    return _build(enc.sym_lut, enc.len_lut, enc.max_bits, _device.cuda_device(device))
+
+
 def _as_tables(tables, enc, dev) -> DecodeTables:
+    """Tables from prepare_decode_tables as they are; a plain (sym_lut,
+    len_lut) pair, as the reference's prepare_decode_tables returns, gets
+    its table block built here."""
     if isinstance(tables, DecodeTables):
         return tables
-    raise TypeError("tables must come from afterimage_b200's prepare_decode_tables")
+    if isinstance(tables, (tuple, list)) and len(tables) == 2:
+        return _build(tables[0], tables[1], enc.max_bits, dev)
+    raise TypeError("tables must be prepare_decode_tables' result or a (sym_lut, len_lut) pair")
 
 
 def decode_gpu_v2(enc, block_chunks: int = 32, device: str = "cuda", *,

@@ -186,3 +186,15 @@ def test_wait_timeout_selftest_validates_on_the_host():
     assert L.aib_selftest_wait_timeout(_lib.WAIT_LIMIT_POLLS + 1, status, None) == _lib.AIB_EINVAL
     assert L.aib_selftest_wait_timeout(1, None, None) == _lib.AIB_EINVAL
     assert b"polls" in L.aib_last_error() or b"null" in L.aib_last_error()
+
+
+def test_decode_tables_unpack_like_the_reference_pair():
+    """No device needed: the tables object is a (sym_lut, len_lut) pair that
+    also carries the library's table block."""
+    import torch
+    from afterimage_b200.runtime.gpu_decode_v2 import DecodeTables
+    sym, ln, blk = torch.zeros(8, dtype=torch.int32), torch.zeros(8, dtype=torch.int8), torch.zeros(16, dtype=torch.uint8)
+    t = DecodeTables(sym, ln, blk, 3)
+    a, b = t
+    assert isinstance(t, tuple) and len(t) == 2 and a is sym and b is ln
+    assert t.block is blk and t.max_bits == 3 and t.sym_lut is sym and t.len_lut is ln

@@ -235,6 +235,19 @@ def test_tables_reused_across_calls_stream_ordered():
     assert np.array_equal(a.cpu().numpy(), G.arr("real_bf16_128x4096", "decoded"))
 
 
+def test_tables_unpack_and_plain_pairs_work_as_in_the_reference():
+    """prepare_decode_tables unpacks to (sym_lut, len_lut) as the reference's
+    does (gpu_decode_v2.py:71-76, :98), and decode_gpu_v2 also takes such a
+    plain pair -- int32 lengths included -- building the table block itself."""
+    from afterimage_b200.runtime.gpu_decode_v2 import decode_gpu_v2, prepare_decode_tables
+    e = G.enc("real_bf16_128x4096")
+    sym, ln = prepare_decode_tables(e)
+    got = decode_gpu_v2(e, tables=(sym, ln.to(torch.int32)))
+    assert np.array_equal(got.cpu().numpy(), G.arr("real_bf16_128x4096", "decoded"))
+    with pytest.raises(TypeError):
+        decode_gpu_v2(e, tables=(sym,))
+
+
 def test_cpu_device_raises_no_fallback():
     from afterimage_b200.runtime.compressed_store import decompress_layer_gpu
     with pytest.raises(RuntimeError, match="no CPU fallback"):
