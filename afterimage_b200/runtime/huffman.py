@@ -90,3 +90,64 @@ def build_decode_lut(table: HuffmanTable, codes: dict[int, int]) -> tuple[np.nda
     _lib.check(L.aib_build_decode_lut(lengths.ctypes.data, cd.ctypes.data, int(table.max_bits),
                                       sym_lut.ctypes.data, len_lut.ctypes.data), "build_decode_lut")
     return sym_lut, len_lut
+
+
+def pack_bits(symbol_stream: np.ndarray, codes: dict[int, int], lengths: dict[int, int]) -> bytes:
+    """MSB-first concatenation of every symbol's code, zero-padded to a whole
+    byte (reference huffman.py:153-192), packed by the library's C++ packer
+    with the whole stream as one chunk. Every symbol must have a code (a
+    symbol without one raises ValueError); at most 2^30 symbols per call."""
+    flat = np.asarray(symbol_stream).reshape(-1)
+    n = int(flat.shape[0])
+    if n == 0:
+        return b""
+    if int(flat.min()) < 0 or int(flat.max()) > 255:
+        raise ValueError("symbols must be in [0, 255]")
+    if n > 1 << 30:
+        raise ValueError("pack_bits packs at most 2^30 symbols per call")
+    flat = np.ascontiguousarray(flat, dtype=np.uint8)
+    ln = np.zeros(256, dtype=np.int32)
+    cd = np.zeros(256, dtype=np.uint32)
+    for s, c in codes.items():
+        if 0 <= int(s) <= 255:
+            ln[int(s)] = int(lengths[s])
+            cd[int(s)] = int(c)
+    L = _lib.load()
+    nbytes = np.zeros(1, dtype=np.int32)
+    offsets = np.zeros(1, dtype=np.int32)
+    total = ctypes.c_int64(0)
+    rc = L.aib_chunk_nbytes(flat.ctypes.data, n, n, ln.ctypes.data, nbytes.ctypes.data, ctypes.addressof(total))
+    if rc != _lib.AIB_OK:
+        raise ValueError("pack_bits: " + L.aib_last_error().decode())
+    out = np.empty(int(total.value) + 8, dtype=np.uint8)
+    _lib.check(L.aib_pack_chunks(flat.ctypes.data, n, n, ln.ctypes.data, cd.ctypes.data, nbytes.ctypes.data,
+                                 offsets.ctypes.data, out.ctypes.data, int(out.shape[0])), "pack_bits")
+    return out[:int(total.value)].tobytes()
+
+
+@dataclasses.dataclass
+class EncodedTensor:
+    """The unchunked encoding (reference huffman.py:243-250)."""
+    packed: bytes
+    table: HuffmanTable
+    codes: dict[int, int]
+    sym_lut: np.ndarray
+    len_lut: np.ndarray
+    n_symbols: int
+    shape: tuple[int, ...]
+
+
+def encode_exponents(exponents, max_bits: int = 16) -> EncodedTensor:
+    """Code from the tensor's own symbol histogram, one packed stream and
+    its decode LUT (reference huffman.py:253-272). The chunked format
+    (huffman_chunked.encode_chunked) is what the decoders read."""
+    import torch
+    flat = (exponents.detach().flatten().cpu().numpy() if isinstance(exponents, torch.Tensor)
+            else np.asarray(exponents).reshape(-1)).astype(np.int64)
+    counts = np.bincount(flat) if flat.size else np.zeros(0, dtype=np.int64)
+    freqs = {int(s): int(c) for s, c in enumerate(counts) if c > 0}
+    lengths = build_lengths(freqs, max_bits=max_bits)
+    table, codes = canonical_codes(lengths)
+    sym_lut, len_lut = build_decode_lut(table, codes)
+    return EncodedTensor(packed=pack_bits(flat, codes, lengths), table=table, codes=codes, sym_lut=sym_lut,
+                         len_lut=len_lut, n_symbols=int(flat.shape[0]), shape=tuple(exponents.shape))
