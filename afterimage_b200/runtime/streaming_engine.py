@@ -82,6 +82,7 @@ class EngineConfig:
     progress: bool = False                  # print generation progress to stderr
     require_pinned_ram: bool = False        # a failed pin of the decoded RAM tier always raises here
     placement_policy: str = "traffic_density"  # the planner's ranking; profiled ones are out of scope
+    quantize: str | None = None             # lossless only: the reference's lossy "q8" is not built here
 
     def __post_init__(self):
         if self.chunk_size < 1:
@@ -130,13 +131,62 @@ class EngineConfig:
         if self.placement_policy not in ("traffic_density", "profiled_knapsack", "critical_path",
                                          "replay_cem", "replay_qubo", "replay_extent_qubo"):
             raise ValueError("unknown placement_policy %r" % (self.placement_policy,))
+        if self.placement_policy in ("profiled_knapsack", "critical_path"):
+            raise ValueError("placement_policy=%r requires critical_path_profile with measured per-tensor "
+                             "costs, which this package does not build" % self.placement_policy)
         if self.placement_policy != "traffic_density":
-            raise ValueError("placement_policy=%r needs measured critical-path profiles or replay plans; "
-                             "this package does not build them (only 'traffic_density')" % self.placement_policy)
+            raise ValueError("placement_policy=%r requires replay_plan_state from calibration traces, which "
+                             "this package does not build" % self.placement_policy)
+        if self.spec_k < 1:
+            raise ValueError("spec_k must be >= 1, got %d" % self.spec_k)
+        if self.quantize is not None:
+            raise ValueError("quantize must be None (lossless); the reference's lossy %r mode is not built "
+                             "in this package" % (self.quantize,))
 
     @property
     def uses_tiered_residency(self) -> bool:
         return self.vram_budget_gb is not None
+
+    @property
+    def is_lossless(self) -> bool:
+        """Bit-identical output (reference config.py:575-580): false only
+        with a chunked head, whose row blocks change the matmul's
+        reduction order."""
+        return self.quantize is None and self.lm_head_slice_rows == 0
+
+    @property
+    def exactness_contract(self) -> str:
+        """The strongest claim this configuration supports (reference
+        config.py:587-595, for the modes built here)."""
+        return "approximate" if not self.is_lossless else "reference_execution_equivalent"
+
+    def to_dict(self) -> dict:
+        return dataclasses.asdict(self)
+
+    @classmethod
+    def from_dict(cls, values: dict) -> "EngineConfig":
+        """Rejects unknown fields, as the reference does (config.py:601-606)."""
+        names = {f.name for f in dataclasses.fields(cls)}
+        unknown = sorted(set(values) - names)
+        if unknown:
+            raise ValueError("unknown EngineConfig fields: %s" % ", ".join(unknown))
+        return cls(**values)
+
+    def fingerprint(self) -> str:
+        """16 hex digits of the SHA-256 of the sorted-key JSON of every field."""
+        import hashlib
+        payload = json.dumps(self.to_dict(), sort_keys=True, separators=(",", ":"))
+        return hashlib.sha256(payload.encode("utf-8")).hexdigest()[:16]
+
+    def describe(self) -> str:
+        """One line: exactness and residency (reference config.py:612-628)."""
+        lossless = ("LOSSLESS (bit-exact output)" if self.is_lossless else
+                    "LOSSY: lm_head_slice_rows=%d -- output is NOT bit-exact" % self.lm_head_slice_rows)
+        if not self.uses_tiered_residency:
+            return lossless + " | residency: legacy fixed policy"
+        return "%s | residency: VRAM %.2f GB%s | io_prefetch_depth=%d" % (
+            lossless, self.vram_budget_gb, (" + RAM %.2f GB" % self.ram_budget_gb) if self.ram_budget_gb else "",
+            self.io_prefetch_depth)
 
 
 @dataclasses.dataclass

@@ -143,3 +143,25 @@ def test_compress_calls_control_per_tensor_and_cancels(tmp_path):
     assert not (tmp_path / "cancelled" / "manifest.json").exists()
     with pytest.raises(ValueError, match="max_workers"):
         compress_model_to_disk("tiny", tmp_path / "bad", max_workers=0, source_dir=str(snap))
+
+
+def test_engine_config_contract_round_trip_and_fingerprint():
+    """is_lossless / exactness_contract / describe / to_dict / from_dict /
+    fingerprint as in the reference (config.py:575-628), for the modes this
+    package builds."""
+    from afterimage_b200.runtime.config import EngineConfig
+    cfg = EngineConfig()
+    assert cfg.quantize is None and cfg.is_lossless and cfg.exactness_contract == "reference_execution_equivalent"
+    assert cfg.describe() == "LOSSLESS (bit-exact output) | residency: legacy fixed policy"
+    chunked = EngineConfig(lm_head_slice_rows=4096, vram_budget_gb=4.0, ram_budget_gb=2.0, io_prefetch_depth=2)
+    assert not chunked.is_lossless and chunked.exactness_contract == "approximate"
+    assert chunked.describe() == ("LOSSY: lm_head_slice_rows=4096 -- output is NOT bit-exact | residency: "
+                                  "VRAM 4.00 GB + RAM 2.00 GB | io_prefetch_depth=2")
+    again = EngineConfig.from_dict(chunked.to_dict())
+    assert again == chunked and again.fingerprint() == chunked.fingerprint() != cfg.fingerprint()
+    assert len(cfg.fingerprint()) == 16 and int(cfg.fingerprint(), 16) >= 0
+    with pytest.raises(ValueError, match="unknown EngineConfig fields: draft_mode"):
+        EngineConfig.from_dict({**cfg.to_dict(), "draft_mode": "model"})
+    for bad in (dict(spec_k=0), dict(quantize="q8")):
+        with pytest.raises(ValueError):
+            EngineConfig(**bad)
