@@ -97,6 +97,68 @@ def test_tiered_residency_is_bit_exact(untied, tiers):
         assert "disk" in kinds or "ram" in kinds, kinds
 
 
+def _budget(manifest, vram_frac, ram_frac=None, slice_elems=1 << 16):
+    """Budgets as fractions of the model's bytes above the planner's fixed
+    headroom (the convention of test_tiered_residency_is_bit_exact)."""
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, engine_headroom_bytes
+    total = sum(v["orig_bytes"] for v in manifest["tensors"].values() if not v.get("row_gather"))
+    head = engine_headroom_bytes(manifest, EngineConfig(decode_slice_elems=slice_elems))
+    kw = dict(vram_budget_gb=(head + vram_frac * total) / 1e9, decode_slice_elems=slice_elems)
+    if ram_frac is not None:
+        kw["ram_budget_gb"] = ram_frac * total / 1e9
+    return kw
+
+
+def test_streamed_lm_head_is_exact_and_never_stays_resident(untied):
+    """With no VRAM left for residency an untied head is on the disk tier:
+    loaded for its own forward and back on the meta device after it
+    (reference tests/test_streaming_engine_gpu.py:531-588)."""
+    cfg, model, snap, store, manifest = untied
+    ids = torch.randint(0, cfg.vocab_size, (1, 6), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits
+    with _engine(snap, store, **_budget(manifest, 0.0)) as eng:
+        assert eng.tier_of("lm_head.weight") == "disk"
+        assert eng.model.lm_head.weight.device.type == "meta"
+        got = eng.forward_logits(ids)
+        assert eng.model.lm_head.weight.device.type == "meta"
+        got2 = eng.forward_logits(ids)
+    assert torch.equal(got, ref) and torch.equal(got2, ref)
+
+
+@pytest.mark.parametrize("slice_elems", [1 << 10, 1 << 14, 1 << 25])
+def test_decode_slice_size_never_changes_decoded_values(untied, slice_elems):
+    """decode_slice_elems bounds decode scratch only: every slicing of the
+    resident tensors gives the same logits (reference :635-663)."""
+    cfg, model, snap, store, manifest = untied
+    ids = torch.randint(0, cfg.vocab_size, (1, 5), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits
+    with _engine(snap, store, **_budget(manifest, 2.0, slice_elems=slice_elems)) as eng:
+        assert "vram" in set(eng._tier.values())
+        got = eng.forward_logits(ids)
+    assert torch.equal(got, ref)
+
+
+def test_compressed_ram_tier_is_exact_and_persists_across_tokens(untied):
+    """Everything but the row-gathered embedding in the compressed RAM tier:
+    the cached compressed tensors stay the same objects from token to token
+    and every forward is exact (reference :476-529)."""
+    cfg, model, snap, store, manifest = untied
+    ids = torch.randint(0, cfg.vocab_size, (1, 5), device="cuda")
+    with torch.no_grad():
+        ref = model(input_ids=ids).logits
+    with _engine(snap, store, ram_tier_format="compressed", **_budget(manifest, 0.0, 2.0)) as eng:
+        ram = {k for k, t in eng._tier.items() if t == "ram"}
+        assert any(k.startswith("model.layers.") for k in ram)
+        cached = dict(eng._ram_cache)
+        got = eng.forward_logits(ids)
+        got2 = eng.forward_logits(ids)
+        assert set(eng._ram_cache) == set(cached)
+        assert all(eng._ram_cache[k] is v for k, v in cached.items())
+    assert torch.equal(got, ref) and torch.equal(got2, ref)
+
+
 @pytest.mark.parametrize("rows", [500, 1536, 4096])
 def test_chunked_lm_head_streams_in_row_blocks(untied, rows):
     """lm_head_slice_rows: the head stays on the meta device and logits are
