@@ -165,3 +165,21 @@ def test_engine_config_contract_round_trip_and_fingerprint():
     for bad in (dict(spec_k=0), dict(quantize="q8")):
         with pytest.raises(ValueError):
             EngineConfig(**bad)
+
+
+def test_progress_lines_only_when_asked(capsys):
+    """EngineConfig.progress: one stderr line per generated token, ended by
+    a newline; silent otherwise."""
+    import time
+    import types
+    from afterimage_b200.runtime.streaming_engine import EngineConfig, StreamingLosslessModel
+    quiet = types.SimpleNamespace(config=EngineConfig())
+    loud = types.SimpleNamespace(config=EngineConfig(progress=True))
+    t0 = time.perf_counter()
+    StreamingLosslessModel._progress(quiet, 1, 3, t0)
+    assert capsys.readouterr().err == ""
+    for i in (1, 2, 3):
+        StreamingLosslessModel._progress(loud, i, 3, t0)
+    StreamingLosslessModel._progress(loud, None, 3, t0)
+    err = capsys.readouterr().err
+    assert err.count("[afterimage_b200] token") == 3 and "token 3/3" in err and err.endswith("\n")
