@@ -18,7 +18,7 @@ Usage:
 With no file names it runs the files of this path: huffman,
 huffman_chunked, compressed_store, sliced_decompress, binstore,
 vram_planner, decode_table_reuse, gpu_decode, gpu_decode_v2,
-compress_pipeline and config.
+compress_pipeline, config and verify.
 """
 from __future__ import annotations
 
@@ -31,7 +31,7 @@ import tempfile
 REPO = pathlib.Path(__file__).resolve().parents[2]
 FILES = ["test_huffman.py", "test_huffman_chunked.py", "test_compressed_store.py", "test_sliced_decompress.py",
          "test_binstore.py", "test_vram_planner.py", "test_decode_table_reuse.py", "test_gpu_decode.py",
-         "test_gpu_decode_v2.py", "test_compress_pipeline.py", "test_config.py"]
+         "test_gpu_decode_v2.py", "test_compress_pipeline.py", "test_config.py", "test_verify.py"]
 MODULES = ["huffman", "huffman_chunked", "gpu_decode", "gpu_decode_v2", "compressed_store", "binstore",
            "vram_planner", "streaming_engine", "verify", "config", "critical_path", "cpu_decode", "directio"]
 
