@@ -325,7 +325,20 @@ struct Reader {
   int nb;
   int wi;      // next word to load (block wi / 4, slot (wi / 4) % kSlots)
   int64_t bi;  // next 16-byte block to request
+  int end;     // bit index of the chunk's end, counted like wi * 32 - nb
 };
+
+// The reference reader stops refilling at the chunk's last byte and shifts
+// in zeros (huffman_chunked.py:225-231, cpu_decode.py:84-88); this reader
+// refills from whatever follows in `packed`. A prefix-code lookup never
+// depends on those bits, but the exact slow path looks up the whole window,
+// so it clears the window bits that lie past the chunk's end first.
+__device__ __forceinline__ uint32_t slow_window(const Reader &r, int max_bits) {
+  uint32_t w = (r.ah >> 16) >> (16 - max_bits);
+  const int rem = r.end - (r.wi * 32 - r.nb);  // chunk bits not yet consumed
+  if (rem < max_bits) w &= rem <= 0 ? 0u : ~((1u << (max_bits - rem)) - 1u);
+  return w;
+}
 
 // entering the block of word wi: its copy has landed; request the one
 // kSlots - 1 blocks ahead
@@ -355,8 +368,9 @@ __device__ __forceinline__ void reader_consume(Reader &r, uint32_t n) {
 }
 
 __device__ __forceinline__ void reader_init(Reader &r, unsigned char *ring, const uint4 *src, int64_t bmax,
-                                            int64_t pos, uint64_t pol) {
+                                            int64_t pos, int64_t nbytes, uint64_t pol) {
   const int64_t b0 = pos >> 4;
+  r.end = static_cast<int>(min(static_cast<int64_t>(pos & 15) * 8 + nbytes * 8, static_cast<int64_t>(INT32_MAX)));
 #pragma unroll
   for (int s = 0; s < kSlots - 1; ++s) cp_async16(ring + s * 16, src + min(b0 + s, bmax), pol);
   r.bi = b0 + kSlots - 1;
@@ -434,15 +448,16 @@ __device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast,
     const int need = active ? static_cast<int>(min(cs, J.e1 - c * cs)) : 0;
 
     Reader rd;
-    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.wi = 0; rd.bi = 0;
+    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.wi = 0; rd.bi = 0; rd.end = 0;
     if (active) {
       int64_t pos = static_cast<int64_t>(J.offs[c - J.chunk_base]) - J.offset_base;
-      const int64_t nbyt = J.nbytes[c - J.chunk_base];
+      int64_t nbyt = J.nbytes[c - J.chunk_base];
       if (pos < 0 || nbyt < 0 || pos + nbyt > J.packed_nbytes) {
         if (status) atomicOr(status, AIB_STATUS_BAD_CHUNK_RANGE);
         pos = 0;
+        nbyt = 0;
       }
-      reader_init(rd, my_stream, src, bmax, pos, pol_keep);
+      reader_init(rd, my_stream, src, bmax, pos, nbyt, pol_keep);
     }
 
     const int max_need = fast ? static_cast<int>(cs)
@@ -490,7 +505,7 @@ __device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast,
           if (__any_sync(__activemask(), ymin == 0u)) {
             if (ymin == 0u) {
               // >= 20 valid bits remain here: the window needs max_bits <= 16
-              const uint32_t w = (rd.ah >> 16) >> (16 - max_bits);
+              const uint32_t w = slow_window(rd, max_bits);
               const uint32_t sy = static_cast<uint32_t>(__ldg(J.sym_lut + w)) & 0xFFu;
               const uint32_t l = static_cast<uint32_t>(static_cast<int>(__ldg(J.len_lut + w))) & 31u;
               reader_consume(rd, l);
@@ -608,6 +623,10 @@ __device__ __forceinline__ bool stage_table(uint2 *s_fast, const uint2 *src, con
   __syncthreads();
   if (cta_wait_gave_up(bar, 0, kWaitLimit)) {
     if (status && threadIdx.x == 0) atomicOr(status, AIB_STATUS_WAIT_TIMEOUT);
+    // The copy may still be in flight: give it a second bounded wait before
+    // the CTA exits and its shared memory goes to another CTA. The launch
+    // has failed either way; its outputs are to be discarded.
+    (void)cta_wait_gave_up(bar, 0, kWaitLimit);
     return false;
   }
   if (*flags != 0) {
@@ -748,16 +767,17 @@ __device__ __forceinline__ void gemv_groups(const GemvJob &G, const uint2 *s_fas
     const uint8_t *smp = G.sm + cl * cs;
     const uint16_t *xp = G.x + static_cast<int64_t>(j) * cs;
     Reader rd;
-    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.wi = 0; rd.bi = 0;
+    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.wi = 0; rd.bi = 0; rd.end = 0;
     if (active) {
       const int64_t c = G.c0 + cl;
       int64_t pos = static_cast<int64_t>(G.offs[c - G.chunk_base]) - G.offset_base;
-      const int64_t nbyt = G.nbytes[c - G.chunk_base];
+      int64_t nbyt = G.nbytes[c - G.chunk_base];
       if (pos < 0 || nbyt < 0 || pos + nbyt > G.packed_nbytes) {
         if (status) atomicOr(status, AIB_STATUS_BAD_CHUNK_RANGE);
         pos = 0;
+        nbyt = 0;
       }
-      reader_init(rd, my_stream, src, bmax, pos, pol_keep);
+      reader_init(rd, my_stream, src, bmax, pos, nbyt, pol_keep);
       for (int q = 0; q < cs; q += 128) prefetch_l2(smp + q);
     }
     const int need = active ? cs : 0;
@@ -778,7 +798,7 @@ __device__ __forceinline__ void gemv_groups(const GemvJob &G, const uint2 *s_fas
         if (__any_sync(__activemask(), ymin == 0u)) {
           if (ymin == 0u) {
             // a code longer than the table: the reference LUT (>= 20 valid bits here)
-            const uint32_t w = (rd.ah >> 16) >> (16 - max_bits);
+            const uint32_t w = slow_window(rd, max_bits);
             const uint32_t sy = static_cast<uint32_t>(__ldg(G.sym_lut + w)) & 0xFFu;
             const uint32_t l = static_cast<uint32_t>(static_cast<int>(__ldg(G.len_lut + w))) & 31u;
             reader_consume(rd, l);
@@ -1238,35 +1258,36 @@ AIB_API int aib_decode_gemv_bf16_batch_noalloc(const aib_gemv_desc *descs, int c
     return AIB_EINVAL;
   }
   if (!descs) return aib_set_error("null descriptor array"), AIB_EINVAL;
-  // the scratch each descriptor needs, checked before any device call
-  int64_t need[AIB_MAX_BATCH];
-  int64_t total = 0;
+  // Each descriptor's area of the array (256-byte aligned), laid out and
+  // checked against the array's size before any device call. The sums stop
+  // at the first area that does not fit, so no bogus range can overflow them.
+  int64_t area[AIB_MAX_BATCH];
+  int64_t end = 0;
   for (int i = 0; i < count; ++i) {
     const aib_stream_desc &d = descs[i].stream;
     if (d.chunk_size < 1) return aib_set_errorf("chunk_size must be >= 1, got %d", d.chunk_size), AIB_EINVAL;
-    if (d.elem_begin < 0 || d.elem_end < d.elem_begin)
+    if (d.n_symbols < 0 || d.elem_begin < 0 || d.elem_end < d.elem_begin || d.elem_end > d.n_symbols)
       return aib_set_error("gemv: bad element range"), AIB_EINVAL;
-    need[i] = (d.elem_end - d.elem_begin + d.chunk_size - 1) / d.chunk_size;
-    total += need[i];
+    const int64_t len = d.elem_end - d.elem_begin;
+    const int64_t need = len / d.chunk_size + (len % d.chunk_size != 0);
+    if (need > AIB_GEMV_SCRATCH_FLOATS - end)
+      return aib_set_errorf("gemv: the batch needs more than the %d scratch floats the library holds "
+                            "(descriptor %d needs %lld at offset %lld)",
+                            AIB_GEMV_SCRATCH_FLOATS, i, (long long)need, (long long)end),
+             AIB_EINVAL;
+    area[i] = end;
+    end += (need + 63) / 64 * 64;  // the next area starts 256-byte aligned
   }
-  if (total > AIB_GEMV_SCRATCH_FLOATS)
-    return aib_set_errorf("gemv: the batch needs %lld scratch floats, the library holds %d", (long long)total,
-                          AIB_GEMV_SCRATCH_FLOATS),
-           AIB_EINVAL;
   // Nothing in the scratch has to start at zero: the decode kernel writes
   // every partial sum of the batch before the row kernel reads it.
   float *base = nullptr;
   const int rc = scratch_address(&base);
   if (rc != AIB_OK) return rc;
   aib_gemv_desc local[AIB_MAX_BATCH];
-  int64_t off = 0;
   for (int i = 0; i < count; ++i) {
     local[i] = descs[i];
-    local[i].partial = base + off;
-    off += (need[i] + 63) / 64 * 64;  // keep each descriptor's area 256-byte aligned
+    local[i].partial = base + area[i];
   }
-  if (off > AIB_GEMV_SCRATCH_FLOATS)
-    return aib_set_error("gemv: the batch's aligned scratch areas do not fit"), AIB_EINVAL;
   return gemv_launch(local, count, d_status, stream);
 }
 

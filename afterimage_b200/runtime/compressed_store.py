@@ -163,9 +163,15 @@ def decompress_layer_gpu(layer: CompressedLayer, device: str = "cuda",
     compressed stream and sign/mantissa bytes is resident at once; each
     slice is one fused decode+recombine launch into the preallocated
     output. The decode tables are built once per call (the kernel needs no
-    per-slice table traffic), which is the behaviour reuse_decode_tables=True
-    asks for; the flag is accepted for compatibility. Stream-ordered on
-    torch.cuda.current_stream(device); no synchronisation."""
+    per-slice table traffic).
+
+    Synchronisation follows the reference: by default the call synchronises
+    (its decoder syncs whenever no tables are passed, gpu_decode_v2.py:115-116)
+    and then reads the device status word, so a corrupt stream raises
+    RuntimeError here. With reuse_decode_tables=True the call stays
+    stream-ordered on torch.cuda.current_stream(device), as the reference's
+    table-reuse path does (compressed_store.py:211-218); a later
+    synchronising call, or _device.check_status, reports any error."""
     dev = _device.cuda_device(device)
     enc = layer.encoded
     n = int(enc.n_symbols)
@@ -176,13 +182,16 @@ def decompress_layer_gpu(layer: CompressedLayer, device: str = "cuda",
         tables = _gd.prepare_decode_tables(enc, dev)
         if n <= max_slice_elems:
             _fused(layer, tables, dev, 0, enc.n_chunks, 0, n, out)
-            return out.reshape(layer.shape)
-        cps = max(1, int(max_slice_elems) // int(enc.chunk_size))
-        for c0 in range(0, enc.n_chunks, cps):
-            c1 = min(c0 + cps, enc.n_chunks)
-            s0 = c0 * enc.chunk_size
-            s1 = min(c1 * enc.chunk_size, n)
-            _fused(layer, tables, dev, c0, c1, s0, s1, out[s0:s1])
+        else:
+            cps = max(1, int(max_slice_elems) // int(enc.chunk_size))
+            for c0 in range(0, enc.n_chunks, cps):
+                c1 = min(c0 + cps, enc.n_chunks)
+                s0 = c0 * enc.chunk_size
+                s1 = min(c1 * enc.chunk_size, n)
+                _fused(layer, tables, dev, c0, c1, s0, s1, out[s0:s1])
+        if not reuse_decode_tables:
+            torch.cuda.synchronize(dev)
+            _device.check_status(dev)
     return out.reshape(layer.shape)
 
 
@@ -190,7 +199,9 @@ def decompress_rows_gpu(layer: CompressedLayer, row_start: int, row_end: int,
                         device: str = "cuda") -> torch.Tensor:
     """Rows [row_start, row_end) of a 2-D compressed tensor (reference
     :254-303): only the covering chunks are uploaded and decoded, and only
-    the asked-for elements are written."""
+    the asked-for elements are written. Synchronises and reads the device
+    status word, as the reference's rows decode syncs (it passes no tables),
+    so a corrupt stream raises RuntimeError here."""
     if len(layer.shape) != 2:
         raise ValueError("decompress_rows_gpu needs a 2D tensor, got shape %r" % (layer.shape,))
     rows, cols = layer.shape
@@ -208,4 +219,6 @@ def decompress_rows_gpu(layer: CompressedLayer, row_start: int, row_end: int,
         out = torch.empty((row_end - row_start) * cols, dtype=torch.bfloat16, device=dev)
         tables = _gd.prepare_decode_tables(enc, dev)
         _fused(layer, tables, dev, c0, c1, e0, e1, out)
+        torch.cuda.synchronize(dev)
+        _device.check_status(dev)
     return out.reshape(row_end - row_start, cols)

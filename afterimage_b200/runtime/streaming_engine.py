@@ -1008,6 +1008,8 @@ class StreamingLosslessModel:
         else:
             out = self.model(input_ids=input_ids, use_cache=False)
         torch.cuda.synchronize(self.device)
+        # the decodes of this forward were stream-ordered; a corrupt stream raises here
+        _device.check_status(self.device)
         wall = time.perf_counter() - t0
         self.stats.compute_seconds += max(0.0, wall - (self.stats.io_seconds - io0)
                                           - (self.stats.decode_seconds - dec0) - (self.stats.h2d_seconds - h2d0))

@@ -551,7 +551,9 @@ class TPDecoder:
             st.graph = g
         for _ in range(todo):
             st.graph.replay()
-        return torch.cat([ids, first.reshape(1, 1), st.tokens[:max_new_tokens - 1].reshape(1, -1)], 1)
+        out = torch.cat([ids, first.reshape(1, 1), st.tokens[:max_new_tokens - 1].reshape(1, -1)], 1)
+        _device.check_status(self.device)  # a corrupt stream in any replayed decode raises here
+        return out
 
     def _prefill_into(self, st: "_StepState", prompt: torch.Tensor) -> None:
         """The prompt pass from an empty cache, leaving its greedy token in
@@ -604,6 +606,7 @@ class TPDecoder:
             nxt = logits[-1:].argmax(-1).reshape(1, 1)
             seq = torch.cat([seq, nxt], 1)
             step = nxt
+        _device.check_status(self.device)  # a corrupt stream in any decode of the run raises here
         return seq
 
 

@@ -102,15 +102,41 @@ def algorithmic_bytes(layers) -> int:
     return total
 
 
-def make_layers(spec, seed: int, device, chunks: dict | None = None):
+def make_layers(spec, seed: int, device, chunks: dict | None = None, keep_source: bool = False):
+    """The workload's tensors, random N(0, 0.02) BF16 (seeded), compressed.
+    With keep_source, also returns each tensor's BF16 source on `device`
+    (what the bit-exact gate compares the decoded layer with)."""
     from afterimage_b200.runtime.compressed_store import compress_layer
     g = torch.Generator(device=device).manual_seed(seed)
-    out = []
+    out, src = [], []
     for i, (name, rows, cols) in enumerate(spec):
         W = (torch.randn(rows, cols, generator=g, device=device) * 0.02).to(torch.bfloat16)
         out.append(compress_layer(W.cpu(), chunk_size=(chunks or {}).get(name, 1024)))
+        if keep_source:
+            src.append(W)
         del W
-    return out
+    return (out, src) if keep_source else out
+
+
+def bit_exact_gate(decoder, descs, outs, sources, layers: list[int]) -> None:
+    """Decodes each listed resident layer with one launch and compares every
+    tensor with its BF16 source bit for bit (raises on a mismatch or a
+    device status error)."""
+    from afterimage_b200.runtime import _device
+    for i in layers:
+        for o in outs:
+            o.fill_(float("nan"))
+        decoder.launch(descs[i], len(outs))
+        torch.cuda.synchronize(decoder.device)
+        _device.check_status(decoder.device)
+        check_outputs(outs, sources[i], "layer %d" % i)
+
+
+def check_outputs(outs, source, what: str) -> None:
+    for o, w in zip(outs, source):
+        if not torch.equal(o.view(torch.int16), w.view(torch.int16)):
+            bad = int((o.view(torch.int16) != w.view(torch.int16)).sum())
+            raise AssertionError("decoded %s differs from its source in %d of %d weights" % (what, bad, w.numel()))
 
 
 class Clocks:
@@ -566,7 +592,9 @@ def dist_setup():
 
 
 def run_reference(args, world, rank):
-    """The reference arm: its CPU decode path on the host cores."""
+    """The reference arm: its CPU decode path (the oracle port of
+    decode_chunks_numba + _recombine, all host threads) on the host cores,
+    over the same workload as our arm: every step decodes the whole layer."""
     if rank != 0:
         return 0
     spec = WORKLOADS[args.workload]
@@ -575,29 +603,24 @@ def run_reference(args, world, rank):
     nbytes = algorithmic_bytes(layers)
     from oracle import oracle as O
     threads = O.max_threads()
-    # each step: one bounded sample = the workload's first tensor (q_proj, 26 M weights, for
-    # the 14B layer)
-    sample = [layers[0]]
-    name, rows, cols = spec[0]
-    for _ in range(1 + args.warmup):
-        O.decompress(sample[0].encoded, sample[0].sign_mantissa.numpy(), threads)
-    sb = algorithmic_bytes(sample)
+    for _ in range(args.warmup):
+        for layer in layers:
+            O.decompress(layer.encoded, layer.sign_mantissa.numpy(), threads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        for layer in sample:
+        for layer in layers:
             O.decompress(layer.encoded, layer.sign_mantissa.numpy(), threads)
     dt = time.perf_counter() - t0
-    v = sb * args.steps / dt / 1e9
+    v = nbytes * args.steps / dt / 1e9
+    sample = ("the whole %s workload (%d tensors, %.1f M weights) per step; oracle port of the reference "
+              "CPU decoder" % (args.workload, len(spec), sum(r * c for _, r, c in spec) / 1e6))
     line = {"metric": METRIC, "value": round(v, 4), "unit": "GB/s", "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
-            "data": "synthetic", "config": dict(bench_config(args, spec, int(nbytes), world),
-                                                sample_per_step="%s tensor (%dx%d)" % (name, rows, cols)),
+            "data": "synthetic", "config": bench_config(args, spec, int(nbytes), world),
             "cpu_baseline": {"value": round(v, 4), "unit": "GB/s", "cores": threads, "kind": "port",
-                             "sample": "%s tensor (%dx%d) per step; oracle port of the reference CPU decoder"
-                                       % (name, rows, cols)},
-            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-            "layer_algorithmic_bytes": nbytes}
+                             "sample": sample},
+            "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
@@ -639,8 +662,11 @@ def main(argv=None) -> int:
     from afterimage_b200.runtime import _device
 
     spec = WORKLOADS[args.workload]
-    host_layers = [make_layers(spec, 1000 * rank + i + 1, dev, WORKLOAD_CHUNKS.get(args.workload))
-                   for i in range(args.layers)]
+    made = [make_layers(spec, 1000 * rank + i + 1, dev, WORKLOAD_CHUNKS.get(args.workload), keep_source=True)
+            for i in range(args.layers)]
+    host_layers = [h for h, _ in made]
+    sources = [s for _, s in made]  # BF16 source of every resident layer, on the device
+    del made
     resident = [[LD.upload_layer(t, dev) for t in layer] for layer in host_layers]
     outs = [torch.empty(r, c, dtype=torch.bfloat16, device=dev) for _, r, c in spec]
     decoder = LD.LayerDecoder(dev)
@@ -648,17 +674,8 @@ def main(argv=None) -> int:
     step_bytes = [algorithmic_bytes(layer) for layer in host_layers]
     torch.cuda.synchronize()
 
-    # correctness gate before timing: every tensor of layer 0 bit-exact
-    decoder.launch(descs[0], len(spec))
-    torch.cuda.synchronize()
-    _device.check_status(dev)
-    for layer, o in zip(host_layers[0], outs):
-        ref_sm = layer.sign_mantissa.numpy()
-        got = o.view(torch.int16).reshape(-1)
-        got_sm = ((((got.to(torch.int32) >> 15) & 1) << 7) | (got.to(torch.int32) & 0x7F)).to(torch.uint8)
-        assert torch.equal(got_sm.cpu(), torch.from_numpy(ref_sm)), "sign/mantissa mismatch"
-    # full exponent check against the encoder input would need the weights; the
-    # parity suite (tests/test_gpu_decode.py) covers bit-exactness.
+    # correctness gate before timing: every tensor of every resident layer bit-exact
+    bit_exact_gate(decoder, descs, outs, sources, list(range(args.layers)))
 
     stream = torch.cuda.current_stream(dev)
     for i in range(args.warmup):
@@ -685,6 +702,12 @@ def main(argv=None) -> int:
     elapsed_ms = t_start.elapsed_time(t_end)
     launch_ms = [a.elapsed_time(b) for a, b in ev]
     _device.check_status(dev)
+    # after the timed loop: the last timed launch's output, then every layer again
+    check_outputs(outs, sources[(args.steps - 1) % args.layers], "layer of the last timed step")
+    bit_exact_gate(decoder, descs, outs, sources, list(range(args.layers)))
+    parity = "bit-exact: every tensor of the %d resident layers equals its BF16 source before and after " \
+             "the timed loop, and the last timed launch's output was checked" % args.layers
+    del sources
     t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -754,6 +777,7 @@ def main(argv=None) -> int:
                          "traffic": profile_traffic(args.workload),
                          "kernel": "aib::decode_kernel<0> (fused decode + recombine)",
                          "avg_launch_ms": round(avg_launch_ms, 5)},
+            "parity": parity,
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,

@@ -197,11 +197,15 @@ int aib_decode_gemv_bf16_batch(const aib_gemv_desc *descs, int count, int32_t *d
  * descriptors, x and y as for aib_decode_gemv_bf16_batch; descs[i].partial
  * is ignored, and the per-chunk partial sums go to a fixed array inside the
  * library instead (AIB_GEMV_SCRATCH_FLOATS floats, 4 MiB, held by every
- * GPU that loads the library until the process exits). A batch needing
- * more than that returns AIB_EINVAL before touching the device; nothing is
- * allocated. The first call on a device looks up the array's device
- * address (cudaGetSymbolAddress) and caches it: make that first call before
- * any stream capture. The array is shared by every call of the process on
+ * GPU that loads the library until the process exits). Each descriptor's
+ * share starts 256-byte aligned, so a batch needs the sum over descriptors
+ * of ceil(chunks / 64) * 64 floats; a batch needing more than the array
+ * returns AIB_EINVAL before touching the device; nothing is allocated. The
+ * first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and caches it: make that first call before any
+ * stream capture. The cached address is not refreshed if the device is
+ * reset (cudaDeviceReset) or its context is recreated later in the
+ * process; do not call this entry point after that. The array is shared by every call of the process on
  * that device and keeps the last call's contents (nothing in it needs to
  * start at zero: each call writes every partial it reads); two calls that
  * overlap on the GPU -- different streams, no ordering between them --

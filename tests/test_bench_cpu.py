@@ -20,7 +20,11 @@ def test_reference_arm_prints_the_contract_line():
     assert line["impl"] == "reference" and line["metric"] == bench.METRIC and line["unit"] == "GB/s"
     assert line["value"] > 0 and line["higher_is_better"] is True
     assert line["config"]["workload"] == "config1-4096x4096"
-    assert line["config"]["sample_per_step"] == "w tensor (4096x4096)"
+    # same workload description as our arm: the whole workload is decoded every step
+    assert line["config"] == bench.bench_config(bench.argparse.Namespace(workload="config1-4096x4096", layers=2),
+                                                bench.WORKLOADS["config1-4096x4096"],
+                                                line["config"]["algorithmic_bytes_per_step"], 1)
+    assert "whole config1-4096x4096 workload" in line["cpu_baseline"]["sample"]
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
     assert line["e2e"] == {"value": line["value"], "unit": "GB/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}

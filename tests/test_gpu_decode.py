@@ -270,6 +270,79 @@ def test_corrupt_chunk_offsets_raise_instead_of_reading_out_of_bounds():
     assert np.array_equal(decode_gpu_v2(e).cpu().numpy(), G.arr("real_bf16_128x4096", "decoded"))
 
 
+def test_corrupt_offsets_raise_through_the_layer_and_rows_entry_points():
+    """The engine's main entry points read the status word on their
+    synchronising path (the reference syncs there, gpu_decode_v2.py:115-116)."""
+    from afterimage_b200.runtime.compressed_store import decompress_layer_gpu, decompress_rows_gpu
+    good = _layer("sliced_512x512")
+    e = good.encoded
+    offs = np.asarray(e.chunk_offsets).copy()
+    offs[3] = 10 ** 9
+    offs[7] = -400
+    bad = type(good)(sign_mantissa=good.sign_mantissa, shape=good.shape,
+                     encoded=type(e)(**{**e.__dict__, "chunk_offsets": offs}))
+    with pytest.raises(RuntimeError, match="corrupt offsets"):
+        decompress_layer_gpu(bad, device="cuda")
+    with pytest.raises(RuntimeError, match="corrupt offsets"):
+        decompress_layer_gpu(bad, device="cuda", max_slice_elems=4096)   # sliced path too
+    with pytest.raises(RuntimeError, match="corrupt offsets"):
+        decompress_rows_gpu(bad, 0, 16, device="cuda")
+    # stream-ordered table reuse does not synchronise; the error surfaces at the next check
+    from afterimage_b200.runtime import _device
+    decompress_layer_gpu(bad, device="cuda", reuse_decode_tables=True)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="corrupt offsets"):
+        _device.check_status(torch.device("cuda", torch.cuda.current_device()))
+    # the context and the status word are healthy afterwards
+    assert np.array_equal(_bits(decompress_layer_gpu(good, device="cuda")), G.arr("sliced_512x512", "recon_bits"))
+
+
+def _decode_unbounded(enc) -> np.ndarray:
+    """The reader WITHOUT the chunk-end bound (refills from the bytes that
+    follow the chunk), to show that a case depends on that bound."""
+    packed = np.asarray(enc.packed)
+    mb, cs = int(enc.max_bits), int(enc.chunk_size)
+    out = np.zeros(enc.n_chunks * cs, dtype=np.uint8)
+    for c in range(enc.n_chunks):
+        pos, buf, nbits = int(enc.chunk_offsets[c]), 0, 0
+        for i in range(cs):
+            while nbits < mb:
+                buf |= (int(packed[pos]) if pos < packed.shape[0] else 0) << (24 - nbits)
+                pos += 1
+                nbits += 8
+            w = (buf >> (32 - mb)) & ((1 << mb) - 1)
+            out[c * cs + i] = int(enc.sym_lut[w]) & 0xFF
+            n = int(enc.len_lut[w])
+            buf = (buf << n) & 0xFFFFFFFF
+            nbits -= n
+    return out[:enc.n_symbols]
+
+
+@pytest.mark.parametrize("chunk_size", [16, 64, 1024])
+def test_non_prefix_lut_reads_zeros_past_the_chunk_end(chunk_size):
+    """A LUT whose symbol depends on every bit of the window (sym = window &
+    0xFF, lengths from the real code): at each chunk's last codes the window
+    reaches past the chunk's bytes into the next chunk's (non-zero) bytes.
+    The reference reader shifts in zeros there (huffman_chunked.py:225-231),
+    and so must the exact slow path."""
+    from afterimage_b200.runtime.compressed_store import compress_layer, decompress_layer_gpu
+    from afterimage_b200.runtime.gpu_decode_v2 import decode_gpu_v2
+    g = torch.Generator().manual_seed(chunk_size)
+    W = (torch.randn(64, 256, generator=g) * 0.02).to(torch.bfloat16)
+    layer = compress_layer(W, chunk_size=chunk_size)
+    e = layer.encoded
+    sym = (np.arange(1 << int(e.max_bits), dtype=np.int64) & 0xFF).astype(np.int32)
+    bad = type(e)(**{**e.__dict__, "sym_lut": sym})
+    want = O.decode_chunked(bad)
+    # the case really reads past chunk ends: the same LUT over unbounded windows differs
+    assert not np.array_equal(_decode_unbounded(bad), want)
+    got = decode_gpu_v2(bad).cpu().numpy()
+    assert np.array_equal(got, want)
+    blayer = type(layer)(sign_mantissa=layer.sign_mantissa, encoded=bad, shape=layer.shape)
+    bits = _bits(decompress_layer_gpu(blayer, device="cuda"))
+    assert np.array_equal(bits.view(np.uint16), O.recombine(want.astype(np.uint8), layer.sign_mantissa.numpy()))
+
+
 def test_non_prefix_lut_is_flagged_and_decoded_exactly_by_the_slow_path():
     """A LUT that is not a prefix-code table (entries not replicated across
     their code's windows): the tables flag it and every lookup goes through

@@ -23,6 +23,29 @@ def test_noalloc_refuses_batches_larger_than_the_scratch_without_a_gpu():
     assert L.aib_decode_gemv_bf16_batch_noalloc(ctypes.byref(g), 0, None, None) == _lib.AIB_EINVAL
 
 
+def test_noalloc_counts_the_aligned_areas_and_rejects_bogus_ranges_without_a_gpu():
+    """Each descriptor's area starts 256-byte aligned: two descriptors whose
+    partial counts sum to exactly the array's size do not fit once the first
+    is padded to 64 floats. Ranges past n_symbols are refused before any
+    sum is formed (no overflow from bogus sizes)."""
+    L = _lib.load()
+    gs = (_lib.GemvDesc * 2)()
+    for g, chunks in zip(gs, (1, _lib.AIB_GEMV_SCRATCH_FLOATS - 1)):
+        g.stream.chunk_size = 16
+        g.stream.n_symbols = g.stream.elem_end = 16 * chunks
+    assert L.aib_decode_gemv_bf16_batch_noalloc(gs, 2, None, None) == _lib.AIB_EINVAL
+    assert b"scratch" in L.aib_last_error()
+    g = _lib.GemvDesc()
+    g.stream.chunk_size = 1
+    g.stream.n_symbols = 16
+    g.stream.elem_end = 2 ** 62   # past n_symbols
+    assert L.aib_decode_gemv_bf16_batch_noalloc(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL
+    assert b"element range" in L.aib_last_error()
+    g.stream.n_symbols = g.stream.elem_end = 2 ** 62   # consistent but far too large
+    assert L.aib_decode_gemv_bf16_batch_noalloc(ctypes.byref(g), 1, None, None) == _lib.AIB_EINVAL
+    assert b"scratch" in L.aib_last_error()
+
+
 @pytest.mark.gpu
 def test_noalloc_matches_caller_scratch_on_two_calls_in_a_row():
     from afterimage_b200.runtime import _device
@@ -34,7 +57,10 @@ def test_noalloc_matches_caller_scratch_on_two_calls_in_a_row():
     L = _lib.load()
     st = _device.status_word(dev)
     stream = torch.cuda.current_stream(dev).cuda_stream
-    shapes = [((1024, 5120), 1024), ((512, 640), 640), ((128, 2176), 1088)]
+    # partial counts 5120, 512, 256 and 3: the last is no multiple of 64, so
+    # the next descriptor's area would start after 61 floats of padding
+    shapes = [((1024, 5120), 1024), ((512, 640), 640), ((128, 2176), 1088), ((3, 1024), 1024),
+              ((64, 512), 512)]
     layers = []
     for i, ((R, C), cs) in enumerate(shapes):
         g = torch.Generator().manual_seed(40 + i)
