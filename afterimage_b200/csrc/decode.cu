@@ -18,8 +18,9 @@
 //     exact slow path through the reference LUT in global memory, so every
 //     decoded symbol equals the reference's LUT result;
 //   * each lane's chunk bytes stream through a per-lane shared-memory ring
-//     of 16-byte blocks filled by cp.async a few blocks ahead; the 64-bit
-//     bit buffer refills 32-bit words straight from that ring;
+//     of 16-byte blocks filled by cp.async a few blocks ahead; each loop
+//     iteration builds a 64-bit window of the stream from three ring words
+//     at the lane's bit position and makes five table lookups in it;
 //   * symbols are flushed four at a time into a per-lane shared-memory
 //     ring; every 64 symbols the warp merges the ring with the sign/mantissa
 //     bytes (the reference's _recombine, compressed_store.py:94-114) and
@@ -27,7 +28,8 @@
 // The decoder uses no tensor cores and no scratch global memory: the
 // exponent never round-trips through HBM. The fused decode -> GEMV kernels
 // further down share the reader and table; they keep one fp32 partial sum
-// per chunk in scratch.
+// per chunk in scratch (their per-lane reader refills its bit buffer a word
+// at a time from the same kind of ring).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -80,9 +82,6 @@ namespace aib {
 #endif
 #ifndef AIB_FAST_BITS
 #define AIB_FAST_BITS 12
-#endif
-#ifndef AIB_AHEAD
-#define AIB_AHEAD 1
 #endif
 // Launches with fewer groups than a wave of warps spread them over every SM
 // (fewer active warps per CTA) instead of filling few CTAs; groups are
@@ -388,18 +387,91 @@ __device__ __forceinline__ void reader_init(Reader &r, unsigned char *ring, cons
   reader_consume(r, static_cast<uint32_t>(pos & 3) * 8);
 }
 
-// Append one table payload (up to four symbols, 8 * count in e.y bits
-// 8..15) to the lane's pending bytes olo:ohi and flush a full word to the
-// ring. Payload bytes beyond the count are zero, so a zero entry is a no-op.
-__device__ __forceinline__ void emit(uint2 e, uint32_t &olo, uint32_t &ohi, int &n8, int &k,
-                                     unsigned char *my_ring) {
+// ---------------------------------------------------------------------------
+// Windowed reader: the lane's position in its chunk is one bit counter, and
+// each loop iteration builds a 64-bit window of the stream from three
+// consecutive 32-bit words of the lane's shared-memory ring (no per-lookup
+// refill, no branch). The ring holds kSlots 16-byte blocks of the chunk plus
+// a two-word guard after the last slot that repeats the first two words of
+// slot 0, so three consecutive words never wrap. A window covers any
+// kLookups table lookups of at most kFastBits bits each plus one exact
+// long-code lookup of up to 16 bits.
+// ---------------------------------------------------------------------------
+#ifndef AIB_LOOKUPS
+#define AIB_LOOKUPS 5
+#endif
+constexpr int kLookups = AIB_LOOKUPS;
+// the window covers kLookups full lookups, or a long-code lookup (up to 16
+// bits) after kLookups - 1 of them
+static_assert(kLookups * kFastBits <= 64 && (kLookups - 1) * kFastBits + 16 <= 64, "a window holds 64 bits");
+static_assert(kSlots >= 4, "the window needs the current and the next block, two more in flight");
+
+struct Window {
+  int pos;   // bits consumed, counted from the first byte of block b0 (the block of the chunk's first byte)
+  int lo;    // the lowest block (relative to b0) the window may still read
+  int end;   // bit index of the chunk's end, same origin as pos
+  int64_t b0;
+};
+
+// Request block j (relative to b0) into its slot; slot 0's first two words
+// also go to the guard. One commit group per block.
+__device__ __forceinline__ void win_request(const Window &r, int j, unsigned char *ring, const uint4 *src,
+                                            int64_t bmax, uint64_t pol) {
+  const int slot = j & (kSlots - 1);
+  const uint4 *g = src + min(r.b0 + j, bmax);
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint.L2::256B [%0], [%1], 16, 16, %2;" ::"r"(
+                   smem_u32(ring + slot * 16)),
+               "l"(g), "l"(pol)
+               : "memory");
+  if (slot == 0)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, 8;" ::"r"(smem_u32(ring + kSlots * 16)), "l"(g)
+                 : "memory");
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void win_init(Window &r, unsigned char *ring, const uint4 *src, int64_t bmax,
+                                         int64_t pos, int64_t nbytes, uint64_t pol) {
+  r.b0 = pos >> 4;
+  r.pos = static_cast<int>(pos & 15) * 8;
+  r.lo = 0;
+  r.end = static_cast<int>(min(static_cast<int64_t>(r.pos) + nbytes * 8, static_cast<int64_t>(INT32_MAX)));
+#pragma unroll
+  for (int j = 0; j < kSlots; ++j) win_request(r, j, ring, src, bmax, pol);
+}
+
+// Before reading the window: when the position has entered a new block, the
+// slot of the block before it is free and takes the block kSlots - 1
+// ahead; then wait until the current and the next block have landed (every
+// request but the newest kSlots - 2). An iteration consumes fewer than 128
+// bits, so the position enters at most one new block per iteration.
+__device__ __forceinline__ void win_stage(Window &r, unsigned char *ring, const uint4 *src, int64_t bmax,
+                                          uint64_t pol) {
+  const int nlo = r.pos >> 7;
+  if (nlo != r.lo) {
+    r.lo = nlo;
+    win_request(r, nlo + kSlots - 1, ring, src, bmax, pol);
+  }
+  cp_async_wait<kSlots - 2>();
+}
+
+// The 64 stream bits from r.pos on, MSB first, as hi:lo.
+__device__ __forceinline__ void win_read(const Window &r, const unsigned char *ring, uint32_t &hi, uint32_t &lo) {
+  const uint32_t *w = reinterpret_cast<const uint32_t *>(ring) + ((r.pos >> 5) & (kSlots * 4 - 1));
+  const uint32_t a0 = bswap(w[0]), a1 = bswap(w[1]), a2 = bswap(w[2]);
+  hi = __funnelshift_l(a1, a0, static_cast<uint32_t>(r.pos));  // shift amount taken mod 32
+  lo = __funnelshift_l(a2, a1, static_cast<uint32_t>(r.pos));
+}
+
+// emit() for the windowed loop: the pending word's high part is always zero
+// before a payload is added (a flush leaves only the spill of the payload
+// that crossed the word), so the spill is assigned rather than merged.
+__device__ __forceinline__ void emit_w(uint2 e, uint32_t &olo, int &n8, int &k, unsigned char *my_ring) {
   olo |= e.x << n8;
-  ohi |= __funnelshift_l(e.x, 0u, static_cast<uint32_t>(n8));
+  const uint32_t spill = __funnelshift_l(e.x, 0u, static_cast<uint32_t>(n8));
   n8 += static_cast<int>(e.y >> 8);
   if (n8 >= 32) {
     *reinterpret_cast<uint32_t *>(my_ring + (k & (kRing - 1))) = olo;
-    olo = ohi;
-    ohi = 0;
+    olo = spill;
     n8 -= 32;
     k += 4;
   }
@@ -426,14 +498,17 @@ __device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast,
   const int max_bits = J.max_bits;
   const uint4 *src = reinterpret_cast<const uint4 *>(J.packed);
   const int64_t bmax = J.packed_cap / 16 - 1;
-  // lane's slot in the merge: each chunk's kPhase symbols are kVecs 8-symbol
-  // vectors; lane covers vector (lane % kVecs) of chunk (lane / kVecs) + kRowsPerIt * it
+  // lane's slot in the interior merge: each chunk's kPhase symbols are kVecs
+  // 8-symbol vectors; at step it the lane covers vector (lane % kVecs) of
+  // chunk it + kIters * (lane / kVecs). The lanes of a half warp then read
+  // two rows kIters apart, whose 8-byte slots fall in disjoint bank pairs.
   constexpr int kVecs = kPhase / 8;
   constexpr int kRowsPerIt = 32 / kVecs;
   constexpr int kIters = kPhase * 32 / 8 / 32;
-  const int64_t lane_elem = (lane / kVecs) * cs + (lane % kVecs) * 8;
-  const int64_t it_stride = kRowsPerIt * cs;
-  const int ring_rd = (lane / kVecs) * kRow + (lane % kVecs) * 8;
+  static_assert(kIters * kRowsPerIt == 32, "the merge covers the warp's 32 chunks");
+  const int64_t lane_elem = (lane / kVecs) * kIters * cs + (lane % kVecs) * 8;
+  const int64_t it_stride = cs;
+  const int ring_rd = (lane / kVecs) * kIters * kRow + (lane % kVecs) * 8;
   const uint64_t pol_keep = policy_keep();
   const uint64_t pol_once = policy_stream();
 
@@ -447,8 +522,8 @@ __device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast,
     const bool fast = J.vec_ok && (cs % kPhase) == 0 && ge0 >= J.e0 && ge0 + 32 * cs <= J.e1;
     const int need = active ? static_cast<int>(min(cs, J.e1 - c * cs)) : 0;
 
-    Reader rd;
-    rd.ah = 0; rd.al = 0; rd.nb = 0; rd.wi = 0; rd.bi = 0; rd.end = 0;
+    Window rd;
+    rd.pos = 0; rd.lo = 0; rd.end = 0; rd.b0 = 0;
     if (active) {
       int64_t pos = static_cast<int64_t>(J.offs[c - J.chunk_base]) - J.offset_base;
       int64_t nbyt = J.nbytes[c - J.chunk_base];
@@ -457,14 +532,14 @@ __device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast,
         pos = 0;
         nbyt = 0;
       }
-      reader_init(rd, my_stream, src, bmax, pos, nbyt, pol_keep);
+      win_init(rd, my_stream, src, bmax, pos, nbyt, pol_keep);
     }
 
     const int max_need = fast ? static_cast<int>(cs)
                               : static_cast<int>(__reduce_max_sync(0xffffffffu, static_cast<unsigned>(need)));
     int k = 0;              // symbols flushed to the ring (multiple of 4)
     int n8 = 0;             // 8 x symbols pending in olo:ohi
-    uint32_t olo = 0, ohi = 0;
+    uint32_t olo = 0;
     const int64_t grp_out = ge0 - J.e0;  // output index of the group's first element (fast path)
 
     for (int ph = 0; ph < max_need; ph += kPhase) {
@@ -479,39 +554,46 @@ __device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast,
         if (ph + kPhase < max_need) prefetch_l2(J.sm + grp_out + static_cast<int64_t>(lane) * cs + ph + kPhase);
       }
       const int target = min(ph + kPhase, need);
-#if AIB_AHEAD
       // Lanes that reach this phase's target keep decoding into the ring's
-      // slack (up to `cap`, never into the region still to be merged), so a
-      // warp waits on its slowest lane once per chunk rather than per phase.
-      const int cap = min(ph + kRing - 12, need);
-      while (__any_sync(0xffffffffu, k + (n8 >> 3) < target)) {
-        if (k + (n8 >> 3) < cap) {
-#else
-      {
-        while (k + (n8 >> 3) < target) {
-#endif
-          if (rd.nb < 32) reader_refill(rd, my_stream, src, bmax, pol_keep);
-          // Two first-level lookups. A window whose first code is longer
-          // than the table (entry 0, a no-op) is resolved below by the
-          // reference LUT, outside the common path.
-          uint32_t ymin = 0xFFFFFFFFu;
+      // slack, up to `cap`: an iteration starting below it writes fewer than
+      // 4 * kLookups + 4 more symbols, never into the region still to be
+      // merged. A warp then waits on its slowest lane about once per chunk.
+      // positions in units of 8 x symbols: 8 * k + n8 counts the symbols decoded
+      const int target8 = 8 * target;
+      const int cap8 = 8 * min(ph + kRing - 4 * kLookups - 4, need);
+      while (__any_sync(0xffffffffu, 8 * k + n8 < target8)) {
+        if (8 * k + n8 < cap8) {
+          win_stage(rd, my_stream, src, bmax, pol_keep);
+          uint32_t hi, lo;
+          win_read(rd, my_stream, hi, lo);
+          // kLookups first-level lookups. A window whose first code is longer
+          // than the table has entry 0: it consumes and emits nothing, so
+          // the lookups after it see the same window (the last one included);
+          // the exact lookup below resolves it.
+          uint32_t acc = 0;  // bits 0..7: bits consumed; bits 8..15: 8 x symbols
+          uint32_t ylast = 0;
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const uint2 e = s_fast[rd.ah >> (32 - kFastBits)];
-            ymin = min(ymin, e.y);
-            reader_consume(rd, e.y & 31u);
-            emit(e, olo, ohi, n8, k, my_ring);
+          for (int u = 0; u < kLookups; ++u) {
+            const uint2 e = s_fast[hi >> (32 - kFastBits)];
+            ylast = e.y;
+            hi = __funnelshift_l(lo, hi, e.y);  // consume e.y & 31 bits
+            lo = __funnelshift_l(0u, lo, e.y);
+            acc += e.y;
+            emit_w(e, olo, n8, k, my_ring);
           }
-          if (__any_sync(__activemask(), ymin == 0u)) {
-            if (ymin == 0u) {
-              // >= 20 valid bits remain here: the window needs max_bits <= 16
-              const uint32_t w = slow_window(rd, max_bits);
+          if (__any_sync(__activemask(), ylast == 0u)) {
+            if (ylast == 0u) {
+              // at least 64 - (kLookups - 1) * kFastBits >= 16 window bits remain
+              uint32_t w = (hi >> 16) >> (16 - max_bits);
+              const int rem = rd.end - rd.pos - static_cast<int>(acc & 0xFFu);
+              if (rem < max_bits) w &= rem <= 0 ? 0u : ~((1u << (max_bits - rem)) - 1u);
               const uint32_t sy = static_cast<uint32_t>(__ldg(J.sym_lut + w)) & 0xFFu;
               const uint32_t l = static_cast<uint32_t>(static_cast<int>(__ldg(J.len_lut + w))) & 31u;
-              reader_consume(rd, l);
-              emit(make_uint2(sy, 8u << 8), olo, ohi, n8, k, my_ring);
+              acc += l;
+              emit_w(make_uint2(sy, 8u << 8), olo, n8, k, my_ring);
             }
           }
+          rd.pos += static_cast<int>(acc & 0xFFu);
         }
       }
       // end of this lane's range: flush the partial word (idempotent)
@@ -525,7 +607,7 @@ __device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast,
         const int64_t ob = grp_out + lane_elem + ph;
 #pragma unroll
         for (int it = 0; it < kIters; ++it) {
-          const uint2 ex = *reinterpret_cast<const uint2 *>(rr + it * kRowsPerIt * kRow);
+          const uint2 ex = *reinterpret_cast<const uint2 *>(rr + it * kRow);
           const int64_t oi = ob + it * it_stride;
           if (MODE == kModeBF16) {
             st_once16(static_cast<uint16_t *>(J.out) + oi, combine8(ex, smv[it]), pol_once);
@@ -944,7 +1026,9 @@ static int make_job(const aib_stream_desc *d, int mode, Job *j, bool *empty) {
     return AIB_EINVAL;
   }
   *empty = false;
-  if (d->chunk_size < 1) return aib_set_errorf("chunk_size must be >= 1, got %d", d->chunk_size), AIB_EINVAL;
+  // the kernels count a chunk's bits in 32-bit integers: 2^26 symbols of at most 16 bits stay in range
+  if (d->chunk_size < 1 || d->chunk_size > (1 << 26))
+    return aib_set_errorf("chunk_size must be in [1, 2^26], got %d", d->chunk_size), AIB_EINVAL;
   if (d->max_bits < 0 || d->max_bits > 16)
     return aib_set_errorf("max_bits must be in [0, 16], got %d", d->max_bits), AIB_EINVAL;
   if (d->n_symbols < 0 || d->elem_begin < 0 || d->elem_end < d->elem_begin || d->elem_end > d->n_symbols)
