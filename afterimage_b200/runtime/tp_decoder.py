@@ -335,6 +335,23 @@ class TPDecoder:
             torch.distributed.all_reduce(x, group=self.group)
         return x
 
+    def _row_parallel(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """x @ w.T for a row-parallel projection (o_proj, down_proj), summed
+        over the ranks. On one rank it is F.linear, the call transformers
+        makes. On several ranks each rank's partial product stays in fp32,
+        the all-reduce sums fp32, and the sum is rounded to BF16 once: a
+        single GEMM's rounding, rather than a rounding of every rank's partial
+        plus one per summation in BF16."""
+        if self.world == 1:
+            return F.linear(x, w)
+        x2 = x.reshape(-1, x.shape[-1])
+        if x2.device.type == "cuda":
+            y = torch.mm(x2, w.t(), out_dtype=torch.float32)
+        else:
+            y = x2.float() @ w.float().t()
+        torch.distributed.all_reduce(y, group=self.group)
+        return y.to(x.dtype).reshape(*x.shape[:-1], w.shape[0])
+
     def _all_gather_last(self, x: torch.Tensor) -> torch.Tensor:
         if self.world == 1:
             return x
@@ -403,10 +420,10 @@ class TPDecoder:
         a = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, scale=self.hd ** -0.5,
                                            enable_gqa=self.nh != self.nkv)
         a = a[0].transpose(0, 1).reshape(T, self.nh * self.hd)
-        x = x + self._all_reduce(F.linear(a, W["self_attn.o_proj.weight"]))
+        x = x + self._row_parallel(a, W["self_attn.o_proj.weight"])
         h = _rms_norm(x, W["post_attention_layernorm.weight"], self.eps)
         m = F.silu(F.linear(h, W["mlp.gate_proj.weight"])) * F.linear(h, W["mlp.up_proj.weight"])
-        return x + self._all_reduce(F.linear(m, W["mlp.down_proj.weight"]))
+        return x + self._row_parallel(m, W["mlp.down_proj.weight"])
 
     def _layer_fused(self, i: int, W: dict, x: torch.Tensor, delta, cache: KVCache,
                      pos: torch.Tensor) -> torch.Tensor:
@@ -423,10 +440,10 @@ class TPDecoder:
         tp_ops.qk_rope_cache(qkv, 1, self.nh, self.nkv, self.hd, qn, kn, self.eps, self.inv_freq, pos, q,
                              cache.k[i], cache.v[i])
         a = tp_ops.decode_attention(q, cache.k[i], cache.v[i], self.nh, self.nkv, self.hd, pos, self.hd ** -0.5)
-        o = self._all_reduce(F.linear(a[None], W["self_attn.o_proj.weight"]))
+        o = self._row_parallel(a[None], W["self_attn.o_proj.weight"])
         h = tp_ops.add_rmsnorm(x, o, W["post_attention_layernorm.weight"], self.eps)
         m = tp_ops.silu_mul(F.linear(h, self._joined(W, *self.JOINS[1])))
-        return self._all_reduce(F.linear(m, W["mlp.down_proj.weight"]))
+        return self._row_parallel(m, W["mlp.down_proj.weight"])
 
     def _layers_fused(self, x: torch.Tensor, cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
         """Every layer for one token, then the final norm; returns the
@@ -608,6 +625,87 @@ class TPDecoder:
             step = nxt
         _device.check_status(self.device)  # a corrupt stream in any decode of the run raises here
         return seq
+
+    @torch.no_grad()
+    def generate_speculative(self, input_ids: torch.Tensor, max_new_tokens: int, draft: "TPDecoder", k: int = 4,
+                             temperature: float = 0.0, generator: torch.Generator | None = None,
+                             stats: dict | None = None) -> torch.Tensor:
+        """Draft/target speculation with a KV cache on both models (the
+        reference's loop, streaming_engine.py:2488-2575; acceptance by
+        verify.py:53-103 through speculative_sample_step). `draft` is another
+        decoder on the same ranks with the same vocabulary (the benchmark
+        pairs the Qwen3-14B shape with a Qwen3-0.6B-shaped draft).
+
+        Each sweep: the draft proposes k tokens one at a time (its
+        single-token steps); the target scores the pending token and the k
+        proposals in ONE (k+1)-token forward at the end of its cache; an
+        accepted prefix plus one correction or bonus token is committed, and
+        both caches are cut back to the committed tokens. The reference
+        instead re-runs the whole sequence through the target every sweep.
+        At temperature <= 0 the accepted tokens are the target's argmax, so
+        the output is greedy decoding's, up to BF16 rounding differences
+        between the (k+1)-token and the one-token forward. Every rank takes
+        the same decisions: the logits are all-gathered, and a generator
+        must be seeded alike on every rank."""
+        from .verify import sample_categorical, speculative_sample_step, temperature_probs
+        if draft.vocab != self.vocab:
+            raise ValueError("the draft's vocabulary (%d) does not match the target's (%d)"
+                             % (draft.vocab, self.vocab))
+        if k < 1:
+            raise ValueError("k must be >= 1")
+        ids = input_ids.reshape(1, -1).to(self.device)
+        P = ids.shape[1]
+        if max_new_tokens < 1:
+            return ids
+        max_len = P + max_new_tokens + k + 2
+        tc = KVCache(self.n_layers, self.nkv, self.hd, max_len, self.device)
+        dc = KVCache(draft.n_layers, draft.nkv, draft.hd, max_len, draft.device)
+        # the first token comes from the target's prompt pass, as in greedy decoding;
+        # the target cache then holds every committed token but the last (pending) one
+        first = temperature_probs(self.forward(ids, tc)[-1], temperature)
+        committed = ids[0].tolist() + [sample_categorical(first, generator) if temperature > 0
+                                       else int(first.argmax())]
+        sweeps = accepted_total = 0
+        while len(committed) - P < max_new_tokens:
+            # draft: catch up on committed tokens it has not seen, then propose k
+            todo = committed[dc.length:]
+            lg = draft.forward(torch.tensor([todo], device=draft.device), dc)[-1]
+            d_tokens, d_probs = [], []
+            for j in range(k):
+                q = temperature_probs(lg, temperature)
+                t = sample_categorical(q, generator) if temperature > 0 else int(q.argmax())
+                d_tokens.append(t)
+                d_probs.append(q)
+                if j + 1 < k:
+                    lg = draft.forward(torch.tensor([[t]], device=draft.device), dc)[-1]
+            # target: the pending token and the k proposals in one forward
+            base = len(committed) - 1
+            tl = self.forward(torch.tensor([[committed[-1]] + d_tokens], device=self.device), tc)
+            t_probs = [temperature_probs(tl[i], temperature) for i in range(k)]
+            bonus = temperature_probs(tl[k], temperature)
+            if temperature > 0:
+                new, n_draft = speculative_sample_step(d_probs, t_probs, d_tokens, bonus, generator)
+            else:
+                # one-hot distributions: accept while the proposal is the target's argmax
+                new, n_draft = [], k
+                for i, t in enumerate(d_tokens):
+                    best = int(t_probs[i].argmax())
+                    new.append(best)
+                    if best != t:
+                        n_draft = i
+                        break
+                else:
+                    new.append(int(bonus.argmax()))
+            committed += new
+            tc.length = base + 1 + n_draft  # cut the rejected proposals (and their KV entries)
+            dc.length = min(dc.length, base + 1 + n_draft)
+            sweeps += 1
+            accepted_total += n_draft
+        if stats is not None:
+            stats.update(sweeps=sweeps, accepted_from_draft=accepted_total, k=k)
+        _device.check_status(self.device)
+        _device.check_status(draft.device)
+        return torch.tensor([committed[:P + max_new_tokens]], device=self.device)
 
 
 _ALIGN = 256

@@ -276,6 +276,22 @@ def synthetic_checkpoint(hf_cfg, seed: int, device):
         yield name, t.cpu()
 
 
+# seeds of the tokens/s runs: the random-init checkpoint and the prompt
+# (tests/golden/engine_tokens_qwen3-0.6b.npz records the reference engine on these)
+TOKENS_WEIGHT_SEED = 14
+TOKENS_PROMPT_SEED = 64
+
+
+def checkpoint_digest(items) -> str:
+    """sha256 over (name, BF16 bits) of every tensor, in checkpoint order."""
+    import hashlib
+    h = hashlib.sha256()
+    for name, t in items:
+        h.update(name.encode())
+        h.update(t.contiguous().view(torch.int16).numpy().tobytes())
+    return h.hexdigest()
+
+
 def model_config(name: str):
     import transformers
     cls, shape, prompt, new, budget, label = MODELS[name]
@@ -466,6 +482,19 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
                        store_build_s=round(time.perf_counter() - t0, 1),
                        store_chunking="chunk_size %d; o_proj %d, down_proj %d (whole chunks per rank up to TP 8)"
                        % (cs, tp_chunk_size(cfg.hidden_size, 8, cs), tp_chunk_size(cfg.intermediate_size, 8, cs)))
+        draft = None
+        if args.model == "qwen3-14b":
+            # the configuration's draft: a Qwen3-0.6B-shaped decoder (same vocabulary), decoded
+            # and resident on every rank, sharded like the target
+            dstore = root / "qwen3-0.6b-draft"
+            if rank == 0:
+                dcfg = model_config("qwen3-0.6b")[0]
+                write_store(synthetic_checkpoint(dcfg, 15, torch.device("cpu")), dstore,
+                            EngineConfig(chunk_size=1024), tied=True, model_id="synthetic/qwen3-0.6b-draft",
+                            progress_every=0)
+            _barrier(world)
+            draft = load_tp_decoder(dstore, model_config("qwen3-0.6b")[0], world, rank, None, dev,
+                                    resident="decoded")
         _barrier(world)
         prompt = torch.randint(0, cfg.vocab_size, (1, P), generator=torch.Generator().manual_seed(64))
         seqs = {}
@@ -549,6 +578,9 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
                                    "note": "tokens_per_s includes the %d-token prompt pass (a captured graph " % P +
                                            "too); step_ms is one replay of the captured single-token step"}
                 dec.release_graphs()
+            if draft is not None and name in ("streamed", "compressed_resident"):
+                info["speculative_draft_0.6B"] = _time_speculative(dec, draft, prompt, args.new_tokens,
+                                                                  seqs[name], world, dev)
             if getattr(dec, "budget_plan", None):
                 info["budget_plan"] = dec.budget_plan
             if resident == "streamed":
@@ -569,6 +601,39 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
         _barrier(world)
         if rank == 0:
             shutil.rmtree(root, ignore_errors=True)
+
+
+def _time_speculative(dec, draft, prompt, new_tokens: int, greedy, world: int, dev, k: int = 4) -> dict:
+    """Draft/target speculation at temperature 0 (TPDecoder.generate_speculative:
+    k proposals from the Qwen3-0.6B-shaped draft, one (k+1)-token target forward
+    per sweep), timed like greedy decoding: prompt pass + new_tokens, CUDA
+    events, max over ranks. Random-init draft and target rarely agree, so
+    this measures the sweep cost and checks the tokens against greedy."""
+    dec.generate_speculative(prompt, 1, draft, k=k)  # warm: draft prompt path, (k+1)-token forward
+    torch.cuda.synchronize()
+    _barrier(world)
+    st = {}
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    seq = dec.generate_speculative(prompt, new_tokens, draft, k=k, stats=st)
+    b.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(a.elapsed_time(b), world, dev)
+    same = bool(torch.equal(seq.cpu(), greedy))
+    out = {"tokens_per_s": round(new_tokens / (ms / 1e3), 3), "s_per_token": round(ms / 1e3 / new_tokens, 4),
+           "k": k, "sweeps": st.get("sweeps"), "accepted_from_draft": st.get("accepted_from_draft"),
+           "tokens_equal_greedy": same, "temperature": 0.0,
+           "note": "random-init draft and target rarely agree: about one token per target sweep"}
+    if not same:
+        # greedy decoding ran the fused single-token step, verification the (k+1)-token
+        # torch math: report where they part and the target's top-2 margin there
+        P = prompt.shape[1]
+        a_, b_ = seq[0].tolist(), greedy[0].tolist()
+        pos = next(i for i in range(len(a_)) if a_[i] != b_[i])
+        lg = dec.forward(greedy[:, :pos].to(dev))[-1].float()
+        top = torch.topk(lg, 2).values
+        out.update(first_divergence=pos - P, top2_margin_at_divergence=round(float(top[0] - top[1]), 5))
+    return out
 
 
 def bench_config(args, spec, step_bytes: int, world: int) -> dict:

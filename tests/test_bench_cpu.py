@@ -52,3 +52,21 @@ def test_cpu_baseline_reports_all_threads_and_one_thread():
     assert cpu["kind"] == "port" and cpu["value"] > 0 and cpu["cores"] >= 1
     one = cpu["single_thread"]
     assert one["cores"] == 1 and one["value"] > 0 and one["sample"].endswith("4096x4096 tensor")
+
+
+def test_reference_engine_token_fixture_is_consistent():
+    """tests/golden/engine_tokens_qwen3-0.6b.npz (the reference engine's own
+    greedy run): its tokens are the argmax of its recorded logits, its
+    margins the top-2 gaps, and its prompt the benchmark's seeded prompt."""
+    import numpy as np
+    import pathlib
+    import torch
+    g = np.load(pathlib.Path(__file__).resolve().parent / "golden" / "engine_tokens_qwen3-0.6b.npz")
+    cfg, P, N, _, _ = bench.model_config("qwen3-0.6b")
+    logits = torch.from_numpy(g["logits_bits"]).view(torch.bfloat16).float()
+    assert logits.shape == (N, cfg.vocab_size)
+    assert g["tokens"].tolist() == logits.argmax(-1).tolist()
+    top = torch.topk(logits, 2, dim=-1).values
+    assert np.allclose(g["top2_margin"], (top[:, 0] - top[:, 1]).numpy())
+    prompt = torch.randint(0, cfg.vocab_size, (1, P), generator=torch.Generator().manual_seed(bench.TOKENS_PROMPT_SEED))
+    assert g["prompt"].tolist() == prompt[0].tolist()

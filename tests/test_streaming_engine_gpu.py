@@ -5,6 +5,8 @@ tiers, prefetch depths, tied/untied heads, KV cache and draft speculation
 (the reference's tests/test_streaming_engine_gpu.py, restated)."""
 import pytest
 import torch
+
+from bf16tol import check_logits
 from safetensors.torch import save_file
 
 pytestmark = pytest.mark.gpu
@@ -173,7 +175,7 @@ def test_chunked_lm_head_streams_in_row_blocks(untied, rows):
         assert eng.model.lm_head.weight.device.type == "meta"
         got = eng.forward_logits(ids)
         assert eng.model.lm_head.weight.device.type == "meta"
-    assert torch.allclose(got.float(), ref.float(), atol=2e-2, rtol=0)
+    check_logits(got[0], ref[0])  # row blocks are separate GEMMs: within 1e-2 or one BF16 step
     assert torch.equal(got.argmax(-1), ref.argmax(-1))
 
 

@@ -9,6 +9,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
+from bf16tol import check_logits
 from oracle import oracle as O
 from afterimage_b200.runtime.compressed_store import compress_layer
 from afterimage_b200.runtime.huffman_chunked import ChunkedEncoded
@@ -189,7 +190,11 @@ def test_tp_forward_matches_transformers_on_cpu(world, tie, arch):
     got = [(r, torch.from_numpy(l), torch.from_numpy(s)) for r, l, s in sorted(got, key=lambda g: g[0])]
     for rank, logits, seq in got:
         assert logits.shape == ref.shape
-        assert torch.allclose(logits, ref, atol=3e-2, rtol=0), (logits - ref).abs().max()
+        # oneDNN's CPU BF16 GEMMs round a column-parallel shard (half the output
+        # width) differently from the whole projection, and those intermediate
+        # roundings propagate through the layers: up to 3 BF16 steps here. The
+        # GPU tests hold the single-GPU decoder to 1e-2 (or one BF16 step).
+        check_logits(logits, ref, atol=2e-2)
         if rank:
             assert torch.equal(logits, got[0][1])  # every rank holds the same gathered logits
     # greedy continuation equals transformers' where the top-2 margin is clear
@@ -251,3 +256,88 @@ def test_plan_resident_layers_fills_budget_beside_working_set():
     assert plan_resident_layers(sizes, 599, 500) == []
     with pytest.raises(ValueError, match="working set"):
         plan_resident_layers(sizes, 400, 500)
+
+
+def _greedy_with_margins(dec, ids, n):
+    """Greedy tokens of `dec` one step at a time, with each step's top-2 margin."""
+    from afterimage_b200.runtime.tp_decoder import KVCache
+    cache = KVCache(dec.n_layers, dec.nkv, dec.hd, ids.shape[1] + n + 4, dec.device)
+    toks, margins, step = [], [], ids
+    for _ in range(n):
+        lg = dec.forward(step, cache)[-1].float()
+        top = torch.topk(lg, 2).values
+        margins.append(float(top[0] - top[1]))
+        toks.append(int(lg.argmax()))
+        step = torch.tensor([[toks[-1]]])
+    return toks, margins
+
+
+def _assert_tokens_match_where_clear(got, want, margins, clear=0.05):
+    for t, mg in enumerate(margins):
+        if mg <= clear:
+            break  # after a near-tie the continuations may legitimately differ
+        assert got[t] == want[t], (t, got, want)
+
+
+def _spec_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.distributed.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        q.put((rank, _speculative_case(world, rank)))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+def _speculative_case(world, rank):
+    """Target and an unrelated draft (another random model of the same
+    vocabulary), and the target as its own draft; greedy tokens and the
+    speculative ones at temperature 0, with the acceptance counts."""
+    cfg, mt = _tiny(11, False, "qwen3")
+    _, md = _tiny(12, False, "qwen3")
+    tgt = TPDecoder(cfg, _shard_weights(mt.state_dict(), world, rank, False), world, rank, None, "cpu")
+    dft = TPDecoder(cfg, _shard_weights(md.state_dict(), world, rank, False), world, rank, None, "cpu")
+    ids = torch.randint(0, cfg.vocab_size, (1, 7), generator=torch.Generator().manual_seed(9))
+    greedy, margins = _greedy_with_margins(tgt, ids, 9)
+    out = {"greedy": greedy, "margins": margins}
+    for name, draft, k in (("unrelated", dft, 3), ("self", tgt, 4)):
+        st = {}
+        seq = tgt.generate_speculative(ids, 9, draft, k=k, stats=st)
+        assert seq.shape == (1, 16) and torch.equal(seq[0, :7], ids[0])
+        out[name] = (seq[0, 7:].tolist(), st)
+    return out
+
+
+def _check_speculative(out):
+    for name in ("unrelated", "self"):
+        toks, st = out[name]
+        _assert_tokens_match_where_clear(toks, out["greedy"], out["margins"])
+        assert st["sweeps"] >= 1 and st["k"] in (3, 4)
+    # the target as its own draft has its proposals accepted
+    assert out["self"][1]["accepted_from_draft"] >= 4
+    assert out["self"][1]["sweeps"] < out["unrelated"][1]["sweeps"]
+
+
+def test_tp_speculative_equals_greedy_at_temperature_zero_on_cpu():
+    """Draft/target speculation in the tensor-parallel decoder (reference
+    streaming_engine.py:2488-2575): at temperature 0 the tokens are the
+    target's greedy tokens wherever its top-2 margin is clear."""
+    _check_speculative(_speculative_case(1, 0))
+
+
+def test_tp_speculative_on_two_gloo_ranks():
+    """Both ranks take the same accept/reject decisions (all-gathered logits)
+    and produce the greedy tokens of a single rank."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_spec_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=300) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got[0]["unrelated"][0] == got[1]["unrelated"][0] and got[0]["self"][0] == got[1]["self"][0]
+    single = _speculative_case(1, 0)
+    _check_speculative(got[0])
+    _assert_tokens_match_where_clear(got[0]["unrelated"][0], single["greedy"], single["margins"])

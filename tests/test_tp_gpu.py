@@ -9,6 +9,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
+from bf16tol import FUSED_STEP_ATOL, check_logits
 from test_streaming_engine_gpu import _store, _tiny
 
 pytestmark = pytest.mark.gpu
@@ -24,6 +25,25 @@ def _ref_greedy(model, ids, n):
             margins.append(float(top[0] - top[1]))
             seq = torch.cat([seq, lg.argmax().reshape(1, 1)], 1)
     return seq, margins
+
+
+def _check_single_token_steps(dec, model, ids, n):
+    """The decoder's single-token steps against transformers' own KV-cache
+    steps, fed the same tokens: logits within 1e-2 (or one BF16 rounding
+    step) at every step for the unfused torch math, within FUSED_STEP_ATOL
+    for the fused layer kernels."""
+    from afterimage_b200.runtime.tp_decoder import KVCache
+    cache = KVCache(dec.n_layers, dec.nkv, dec.hd, ids.shape[1] + n + 2, dec.device)
+    pkv = None
+    step = ids
+    with torch.no_grad():
+        for _ in range(n):
+            out = model(input_ids=step, past_key_values=pkv, use_cache=True)
+            pkv = out.past_key_values
+            ref = out.logits[0, -1].float()
+            got = dec.forward(step, cache)[-1].float()
+            check_logits(got, ref, atol=FUSED_STEP_ATOL if dec.fused else 1e-2)
+            step = ref.argmax().reshape(1, 1)
 
 
 def _check_greedy(seq, ref_seq, margins, n_prompt):
@@ -61,7 +81,8 @@ def test_tp_single_gpu_matches_transformers(stores, resident, kw, which):
     with torch.no_grad():
         ref = model(input_ids=ids).logits[0].float()
     got = dec.forward(ids).float()
-    assert torch.allclose(got, ref, atol=2e-2, rtol=0), float((got - ref).abs().max())
+    check_logits(got, ref)
+    _check_single_token_steps(dec, model, ids, 4)
     seq = dec.generate_greedy(ids, 5)
     ref_seq, margins = _ref_greedy(model, ids, 5)
     _check_greedy(seq, ref_seq, margins, 11)
@@ -97,7 +118,8 @@ def test_tp_tied_head_matches_transformers(tied_store, resident, kw):
     with torch.no_grad():
         ref = model(input_ids=ids).logits[0].float()
     got = dec.forward(ids).float()
-    assert torch.allclose(got, ref, atol=2e-2, rtol=0), float((got - ref).abs().max())
+    check_logits(got, ref)
+    _check_single_token_steps(dec, model, ids, 4)
     ref_seq, margins = _ref_greedy(model, ids, 5)
     _check_greedy(dec.generate_greedy(ids, 5), ref_seq, margins, 10)
     if resident != "streamed":
@@ -238,8 +260,35 @@ def test_tp_two_gpus_nccl_matches_transformers(stores, resident):
         ref = model(input_ids=ids.to("cuda:0")).logits[0].float().cpu()
     for rank, logits, seq, gseq in got:
         logits = torch.from_numpy(logits)
-        assert torch.allclose(logits, ref, atol=3e-2, rtol=0), float((logits - ref).abs().max())
+        check_logits(logits, ref)
     ref_seq, margins = _ref_greedy(model, ids.to("cuda:0"), 5)
     _check_greedy(torch.from_numpy(got[0][2]), ref_seq.cpu(), margins, 11)
     _check_greedy(torch.from_numpy(got[0][3]), ref_seq.cpu(), margins, 11)
     assert (got[0][3] == got[1][3]).all()  # ranks agree
+
+
+@pytest.mark.parametrize("resident", ["compressed", "streamed"])
+def test_tp_speculative_decoding_equals_greedy_on_gpu(stores, resident):
+    """Draft/target speculation in the tensor-parallel decoder at temperature
+    0 (reference streaming_engine.py:2488-2575): the compressed or streamed
+    target verifies k proposals in one (k+1)-token forward; the tokens are
+    the target's greedy tokens wherever its top-2 margin is clear, for an
+    unrelated random draft and for the target as its own draft (whose
+    proposals are accepted)."""
+    from afterimage_b200.runtime.tp_decoder import TPDecoder, load_tp_decoder
+    cfg, model, store, tp_store = stores
+    dec = load_tp_decoder(tp_store, cfg, 1, 0, None, "cuda", resident=resident)
+    _, other = _tiny(tie=False, seed=77, layers=2)
+    unrelated = TPDecoder(cfg, {k: v.to("cuda") for k, v in other.state_dict().items()}, 1, 0, None, "cuda")
+    itself = load_tp_decoder(tp_store, cfg, 1, 0, None, "cuda", resident="decoded")
+    ids = torch.randint(0, cfg.vocab_size, (1, 9), device="cuda", generator=torch.Generator(device="cuda").manual_seed(3))
+    ref_seq, margins = _ref_greedy(model.to("cuda"), ids, 8)
+    for draft, k in ((unrelated, 3), (itself, 4)):
+        st = {}
+        seq = dec.generate_speculative(ids, 8, draft, k=k, stats=st)
+        assert seq.shape == (1, 17)
+        _check_greedy(seq, ref_seq, margins, 9)
+        if draft is itself:
+            assert st["accepted_from_draft"] >= 4 and st["sweeps"] <= 4
+    if resident == "streamed":
+        dec.close()
