@@ -99,6 +99,9 @@ SIGNATURES = [
     ("aib_qk_rope_cache_bf16", CI, [P, CI, CI, CI, CI, P, P, ctypes.c_float, P, P, P, P, P, I64, P]),
     ("aib_decode_attention_bf16", CI, [P, P, P, CI, CI, CI, I64, P, ctypes.c_float, P, P]),
     ("aib_silu_mul_bf16", CI, [P, P, I64, I64, P]),
+    ("aib_gemv_bf16", CI, [P, I64, P, I64, P, I64, I64, I64, CI, CI, P]),
+    ("aib_gemm_bf16_tc", CI, [P, I64, P, I64, P, I64, I64, I64, I64, P, I64, P, P]),
+    ("aib_gemm_bf16_tc_workspace_floats", I64, [I64, I64, I64]),
 ]
 
 

@@ -85,72 +85,3 @@ def decode_gemv(resident, x: torch.Tensor, rows: tuple[int, int] | None = None,
     if synchronize:
         _device.check_status(dev)
     return y
-
-
-def _compare(spec, chunks: dict, device="cuda", reps: int = 50) -> dict:
-    """Times one layer's single-token projections: one batched decode
-    launch followed by F.linear per tensor, against the fused kernel (per
-    dependent launch group, and all tensors in one launch)."""
-    import torch.nn.functional as F
-    from .compressed_store import compress_layer
-    from .layer_decode import LayerDecoder, upload_layer
-    dev = _device.cuda_device(device)
-    g = torch.Generator(device=dev).manual_seed(7)
-    res = []
-    for name, r, c in spec:
-        W = (torch.randn(r, c, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        res.append(upload_layer(compress_layer(W.cpu(), chunk_size=chunks.get(name, 1024)), dev))
-    outs = [torch.empty(r, c, dtype=torch.bfloat16, device=dev) for _, r, c in spec]
-    dec = LayerDecoder(dev)
-    descs = dec.descriptors(res, outs)
-    xs = [torch.randn(c, device=dev, generator=g).to(torch.bfloat16) for _, _, c in spec]
-    ys = [torch.empty(r, dtype=torch.bfloat16, device=dev) for _, r, _ in spec]
-    parts = [torch.empty(r * c // int(rr.encoded.chunk_size), dtype=torch.float32, device=dev)
-             for rr, (_, r, c) in zip(res, spec)]
-    gd = [gemv_desc(rr.stream, rr.tables, rr.encoded, 0, r * c, rr.sign_mantissa, c, x, p, y)
-          for rr, (_, r, c), x, p, y in zip(res, spec, xs, parts, ys)]
-    names = [n for n, _, _ in spec]
-    groups = [[names.index(n) for n in grp if n in names]
-              for grp in (("q_proj", "k_proj", "v_proj"), ("o_proj",), ("gate_proj", "up_proj"), ("down_proj",))]
-    batches = [GemvBatch([gd[i] for i in grp], dev) for grp in groups if grp]
-    one = GemvBatch(gd, dev)
-
-    def timed(fn):
-        for _ in range(5):
-            fn()
-        torch.cuda.synchronize(dev)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        for _ in range(reps):
-            fn()
-        b.record()
-        torch.cuda.synchronize(dev)
-        return a.elapsed_time(b) / reps
-
-    t_dec = timed(lambda: dec.launch(descs, len(spec)))
-    t_lin = timed(lambda: [F.linear(x[None], o) for x, o in zip(xs, outs)])
-    t_groups = timed(lambda: [bt.launch() for bt in batches])
-    t_one = timed(one.launch)
-    _device.check_status(dev)
-    return {"weights": sum(r * c for _, r, c in spec), "decode_ms": round(t_dec, 4), "linear_ms": round(t_lin, 4),
-            "unfused_ms": round(t_dec + t_lin, 4), "fused_4_launches_ms": round(t_groups, 4),
-            "fused_one_launch_ms": round(t_one, 4)}
-
-
-def main() -> None:
-    """python -m afterimage_b200.runtime.decode_gemv: fused vs unfused
-    single-token projections of a Qwen3-14B-shaped layer (whole, TP-ready
-    chunking, and one rank of TP 8); one JSON line per case."""
-    import json
-    layer = [("q_proj", 5120, 5120), ("k_proj", 1024, 5120), ("v_proj", 1024, 5120), ("o_proj", 5120, 5120),
-             ("gate_proj", 17408, 5120), ("up_proj", 17408, 5120), ("down_proj", 5120, 17408)]
-    rank8 = [("q_proj", 640, 5120), ("k_proj", 128, 5120), ("v_proj", 128, 5120), ("o_proj", 5120, 640),
-             ("gate_proj", 2176, 5120), ("up_proj", 2176, 5120), ("down_proj", 5120, 1088)]
-    tp = {"o_proj": 640, "down_proj": 1088}
-    for name, spec, chunks in (("qwen3-14b-layer", layer, {}), ("qwen3-14b-layer-tp8-chunks", layer, tp),
-                               ("qwen3-14b-rank-of-tp8", rank8, tp)):
-        print(json.dumps({"case": name, **_compare(spec, chunks)}), flush=True)
-
-
-if __name__ == "__main__":
-    main()

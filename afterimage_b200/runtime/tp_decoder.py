@@ -335,6 +335,30 @@ class TPDecoder:
             torch.distributed.all_reduce(x, group=self.group)
         return x
 
+    # projections at least this many output rows wide run on this package's kernels in the
+    # fused mode (measured on B200: at or above cuBLAS from here on up, below it for narrower ones)
+    OWN_KERNEL_MIN_ROWS = 16384
+
+    def _proj(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """x @ w.T for a column-parallel projection or the head. In the fused
+        mode a wide projection (>= OWN_KERNEL_MIN_ROWS output rows: gate/up,
+        the vocabulary head) runs on csrc/gemv.cu for up to 8 tokens and on
+        the tcgen05 tensor-core GEMM (csrc/gemm_tc.cu) for 9..64 tokens; both
+        keep fp32 sums and round once. Everything else, and the unfused mode,
+        is F.linear, the call transformers makes."""
+        if self.fused and w.shape[0] >= self.OWN_KERNEL_MIN_ROWS and w.dim() == 2 and w.stride(-1) == 1 \
+                and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16:
+            from . import tp_ops
+            x2 = x.reshape(-1, x.shape[-1])
+            T, K = x2.shape
+            if x2.stride(-1) == 1 and K % 8 == 0 and w.stride(0) % 8 == 0 and x2.stride(0) % 8 == 0 \
+                    and x2.data_ptr() % 16 == 0 and w.data_ptr() % 16 == 0:
+                if T <= 8:
+                    return tp_ops.gemv(x2, w).reshape(*x.shape[:-1], w.shape[0])
+                if T <= 64 and K % 64 == 0:
+                    return tp_ops.gemm_tc(x2, w).reshape(*x.shape[:-1], w.shape[0])
+        return F.linear(x, w)
+
     def _row_parallel(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """x @ w.T for a row-parallel projection (o_proj, down_proj), summed
         over the ranks. On one rank it is F.linear, the call transformers
@@ -422,7 +446,7 @@ class TPDecoder:
         a = a[0].transpose(0, 1).reshape(T, self.nh * self.hd)
         x = x + self._row_parallel(a, W["self_attn.o_proj.weight"])
         h = _rms_norm(x, W["post_attention_layernorm.weight"], self.eps)
-        m = F.silu(F.linear(h, W["mlp.gate_proj.weight"])) * F.linear(h, W["mlp.up_proj.weight"])
+        m = F.silu(self._proj(h, W["mlp.gate_proj.weight"])) * self._proj(h, W["mlp.up_proj.weight"])
         return x + self._row_parallel(m, W["mlp.down_proj.weight"])
 
     def _layer_fused(self, i: int, W: dict, x: torch.Tensor, delta, cache: KVCache,
@@ -442,7 +466,7 @@ class TPDecoder:
         a = tp_ops.decode_attention(q, cache.k[i], cache.v[i], self.nh, self.nkv, self.hd, pos, self.hd ** -0.5)
         o = self._row_parallel(a[None], W["self_attn.o_proj.weight"])
         h = tp_ops.add_rmsnorm(x, o, W["post_attention_layernorm.weight"], self.eps)
-        m = tp_ops.silu_mul(F.linear(h, self._joined(W, *self.JOINS[1])))
+        m = tp_ops.silu_mul(self._proj(h, self._joined(W, *self.JOINS[1])))
         return self._row_parallel(m, W["mlp.down_proj.weight"])
 
     def _layers_fused(self, x: torch.Tensor, cache: KVCache, pos: torch.Tensor) -> torch.Tensor:
@@ -603,7 +627,7 @@ class TPDecoder:
     def head_logits(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's vocab shard of the logits."""
         head = self.w.get("lm_head.weight", None)
-        return F.linear(x, self.weight("lm_head.weight") if head is not None else self.full_embed_shard())
+        return self._proj(x, self.weight("lm_head.weight") if head is not None else self.full_embed_shard())
 
     def full_embed_shard(self) -> torch.Tensor:
         """Tied head: this rank's vocab rows of the (replicated) embedding."""
@@ -1075,7 +1099,7 @@ class CompressedTPDecoder(TPDecoder):
                 self._desc_cache[key] = plan
             d, wv = plan
             self.decoder.launch(d, 1)
-            out[:, r0:r1] = F.linear(x, wv)
+            out[:, r0:r1] = self._proj(x, wv)
         return out
 
     def decode_bytes_per_forward(self) -> int:

@@ -84,4 +84,46 @@ def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Te
     return out
 
 
-__all__ = ["add_rmsnorm", "qk_rope_cache", "decode_attention", "silu_mul"]
+def gemv(x: torch.Tensor, w: torch.Tensor, out_dtype=torch.bfloat16, out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [m, k] (m <= 8 rows) times w.T, w [n, k] row-major BF16 (csrc/gemv.cu):
+    returns [m, n] in BF16 (one rounding of the fp32 sum) or fp32."""
+    x2 = x.reshape(-1, x.shape[-1])
+    m, k = x2.shape
+    n = w.shape[0]
+    if x2.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or w.dim() != 2 or w.shape[1] != k:
+        raise ValueError("gemv needs bf16 x [m, k] and w [n, k]")
+    if x2.stride(-1) != 1 or w.stride(-1) != 1:
+        raise ValueError("gemv needs unit stride along k")
+    if out is None:
+        out = torch.empty(m, n, dtype=out_dtype, device=x.device)
+    L = _lib.load()
+    _lib.check(L.aib_gemv_bf16(w.data_ptr(), w.stride(0), x2.data_ptr(), x2.stride(0), out.data_ptr(),
+                               out.stride(0), n, k, m, int(out.dtype == torch.float32), _stream(x)), "gemv")
+    return out.reshape(*x.shape[:-1], n)
+
+
+def gemm_tc(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """x [m, k] (1 <= m <= 256 rows) times w.T, w [n, k] row-major BF16, on the
+    tensor cores (csrc/gemm_tc.cu); returns BF16 [m, n]. k must be a
+    multiple of 64. Raises RuntimeError if a bounded wait in the kernel gave
+    up (the status word is read: this synchronises)."""
+    from . import _device
+    x2 = x.reshape(-1, x.shape[-1])
+    m, k = x2.shape
+    n = w.shape[0]
+    if x2.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or w.dim() != 2 or w.shape[1] != k:
+        raise ValueError("gemm_tc needs bf16 x [m, k] and w [n, k]")
+    if x2.stride(-1) != 1 or w.stride(-1) != 1:
+        raise ValueError("gemm_tc needs unit stride along k")
+    if out is None:
+        out = torch.empty(m, n, dtype=torch.bfloat16, device=x.device)
+    L = _lib.load()
+    need = int(L.aib_gemm_bf16_tc_workspace_floats(m, n, k))
+    ws = torch.empty(max(need, 1), dtype=torch.float32, device=x.device)
+    _lib.check(L.aib_gemm_bf16_tc(w.data_ptr(), w.stride(0), x2.data_ptr(), x2.stride(0), out.data_ptr(),
+                                  out.stride(0), m, n, k, ws.data_ptr(), need,
+                                  _device.status_word(x.device).data_ptr(), _stream(x)), "gemm_tc")
+    return out.reshape(*x.shape[:-1], n)
+
+
+__all__ = ["add_rmsnorm", "qk_rope_cache", "decode_attention", "silu_mul", "gemv", "gemm_tc"]

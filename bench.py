@@ -636,6 +636,111 @@ def _time_speculative(dec, draft, prompt, new_tokens: int, greedy, world: int, d
     return out
 
 
+def _timed_ms(fn, dev, reps: int = 50) -> float:
+    for _ in range(5):
+        fn()
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        fn()
+    b.record()
+    torch.cuda.synchronize(dev)
+    return a.elapsed_time(b) / reps
+
+
+def projections_compare(spec, chunks: dict, dev) -> dict:
+    """One layer's single-token projections (the seven tensors): one batched
+    decode launch followed by F.linear per tensor (cuBLAS), against the fused
+    decode -> GEMV kernel (per dependent launch group, and all tensors in one
+    launch)."""
+    import torch.nn.functional as F
+    from afterimage_b200.runtime.compressed_store import compress_layer
+    from afterimage_b200.runtime.decode_gemv import GemvBatch, gemv_desc
+    from afterimage_b200.runtime.layer_decode import LayerDecoder, upload_layer
+    from afterimage_b200.runtime import _device
+    g = torch.Generator(device=dev).manual_seed(7)
+    res = []
+    for name, r, c in spec:
+        W = (torch.randn(r, c, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        res.append(upload_layer(compress_layer(W.cpu(), chunk_size=chunks.get(name, 1024)), dev))
+    outs = [torch.empty(r, c, dtype=torch.bfloat16, device=dev) for _, r, c in spec]
+    dec = LayerDecoder(dev)
+    descs = dec.descriptors(res, outs)
+    xs = [torch.randn(c, device=dev, generator=g).to(torch.bfloat16) for _, _, c in spec]
+    ys = [torch.empty(r, dtype=torch.bfloat16, device=dev) for _, r, _ in spec]
+    parts = [torch.empty(r * c // int(rr.encoded.chunk_size), dtype=torch.float32, device=dev)
+             for rr, (_, r, c) in zip(res, spec)]
+    gd = [gemv_desc(rr.stream, rr.tables, rr.encoded, 0, r * c, rr.sign_mantissa, c, x, p, y)
+          for rr, (_, r, c), x, p, y in zip(res, spec, xs, parts, ys)]
+    names = [n for n, _, _ in spec]
+    groups = [[names.index(n) for n in grp if n in names]
+              for grp in (("q_proj", "k_proj", "v_proj"), ("o_proj",), ("gate_proj", "up_proj"), ("down_proj",))]
+    batches = [GemvBatch([gd[i] for i in grp], dev) for grp in groups if grp]
+    one = GemvBatch(gd, dev)
+    t_dec = _timed_ms(lambda: dec.launch(descs, len(spec)), dev)
+    t_lin = _timed_ms(lambda: [F.linear(x[None], o) for x, o in zip(xs, outs)], dev)
+    t_groups = _timed_ms(lambda: [bt.launch() for bt in batches], dev)
+    t_one = _timed_ms(one.launch, dev)
+    _device.check_status(dev)
+    return {"weights": sum(r * c for _, r, c in spec), "decode_ms": round(t_dec, 4), "linear_ms": round(t_lin, 4),
+            "unfused_ms": round(t_dec + t_lin, 4), "fused_4_launches_ms": round(t_groups, 4),
+            "fused_one_launch_ms": round(t_one, 4)}
+
+
+def projections_kernels(dev) -> list:
+    """The dense projections of a decoded Qwen3-14B layer (joined q/k/v, o,
+    joined gate/up, down) and the vocabulary head, through cuBLAS (F.linear)
+    and through this package's kernels: the BF16 GEMV (csrc/gemv.cu) for 1
+    and 5 tokens, the tcgen05 tensor-core GEMM (csrc/gemm_tc.cu) for 16 and
+    64 tokens. Several distinct weights per shape are used round-robin so the
+    L2 does not hold them; GB/s counts weights + activations + outputs."""
+    import torch.nn.functional as F
+    from afterimage_b200.runtime import tp_ops
+    peak, _ = measured_peak()
+    shapes = {"qkv": (7168, 5120), "o": (5120, 5120), "gate_up": (34816, 5120), "down": (5120, 17408),
+              "head": (151936, 5120)}
+    out = []
+    for m in (1, 5, 16, 64):
+        own = tp_ops.gemv if m <= 8 else tp_ops.gemm_tc
+        for name, (n, k) in shapes.items():
+            ws = [(torch.randn(n, k, device=dev) * 0.02).to(torch.bfloat16)
+                  for _ in range(max(2, int(4e8 // (n * k * 2)) + 1))]
+            x = torch.randn(m, k, device=dev).to(torch.bfloat16)
+            it = [0]
+
+            def cub():
+                it[0] += 1
+                return F.linear(x, ws[it[0] % len(ws)])
+
+            def mine():
+                it[0] += 1
+                return own(x, ws[it[0] % len(ws)])
+            tc, to = _timed_ms(cub, dev), _timed_ms(mine, dev)
+            nb = n * k * 2 + m * k * 2 + m * n * 2
+            out.append({"tokens": m, "projection": name, "n": n, "k": k,
+                        "kernel": "gemv" if m <= 8 else "tcgen05 gemm", "cublas_ms": round(tc, 4),
+                        "own_ms": round(to, 4), "own_gbps": round(nb / to / 1e6, 1),
+                        "own_frac_of_hbm": round(nb / to / 1e6 / peak, 3),
+                        "cublas_frac_of_hbm": round(nb / tc / 1e6 / peak, 3)})
+            del ws
+    return out
+
+
+def run_projections(dev) -> int:
+    """`bench.py --projections`: one JSON line per case (not the benchmark line)."""
+    layer = QWEN3_14B_LAYER
+    rank8 = [("q_proj", 640, 5120), ("k_proj", 128, 5120), ("v_proj", 128, 5120), ("o_proj", 5120, 640),
+             ("gate_proj", 2176, 5120), ("up_proj", 2176, 5120), ("down_proj", 5120, 1088)]
+    tp = {"o_proj": 640, "down_proj": 1088}
+    for name, spec, chunks in (("qwen3-14b-layer", layer, {}), ("qwen3-14b-layer-tp8-chunks", layer, tp),
+                               ("qwen3-14b-rank-of-tp8", rank8, tp)):
+        print(json.dumps({"case": "decode->gemv " + name, **projections_compare(spec, chunks, dev)}), flush=True)
+    for row in projections_kernels(dev):
+        print(json.dumps(row), flush=True)
+    return 0
+
+
 def bench_config(args, spec, step_bytes: int, world: int) -> dict:
     """The workload description both arms print (same keys and values)."""
     return {"workload": args.workload, "tensors": [n for n, _, _ in spec],
@@ -708,6 +813,9 @@ def main(argv=None) -> int:
                     help="greedy tokens per generation (default: the model configuration's)")
     ap.add_argument("--model", default="qwen3-14b", choices=sorted(MODELS),
                     help="decoder configuration of the tokens/s measurements")
+    ap.add_argument("--projections", action="store_true",
+                    help="instead of the benchmark: time one layer's projections (decode + cuBLAS, fused "
+                         "decode->GEMV, this package's GEMV and tensor-core GEMM against cuBLAS)")
     ap.add_argument("--no-tp-tokens", action="store_true",
                     help="skip the tensor-parallel tokens/s measurement (its store of the --model shape "
                          "is written to /dev/shm)")
@@ -723,6 +831,11 @@ def main(argv=None) -> int:
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
+    if args.projections:
+        rc = run_projections(dev) if rank == 0 else 0
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return rc
     from afterimage_b200.runtime import layer_decode as LD
     from afterimage_b200.runtime import _device
 

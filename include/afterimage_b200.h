@@ -238,6 +238,35 @@ int aib_decode_attention_bf16(const void *q, const void *k_cache, const void *v_
 /* gate_up [T, 2I] (gate then up per row) -> out [T, I] = bf16(bf16(silu(gate)) * up). */
 int aib_silu_mul_bf16(const void *gate_up, void *out, int64_t T, int64_t I, void *stream);
 
+/* Y[i, r] = sum_j X[i, j] * W[r, j] for i < m (1..8 tokens), r < n, j < k:
+ * the projections that consume a decoded layer when few tokens pass
+ * through it (a greedy step; the k + 1 tokens of a speculative verification).
+ * Replaces, for these shapes, the nn.Linear / F.linear the reference calls
+ * on decoded weights (afterimage/runtime/streaming_engine.py:1871-1915,
+ * :2330). W row-major [n, k] with row stride ldw, X [m, k] with row stride
+ * ldx (BF16, 16-byte aligned, k, ldw and ldx multiples of 8); Y [m, n] with
+ * row stride ldy, BF16 (rounded once from the fp32 sum) or fp32 when
+ * out_fp32 is set. Work is enqueued on `stream`. */
+int aib_gemv_bf16(const void *w, int64_t ldw, const void *x, int64_t ldx, void *y, int64_t ldy, int64_t n,
+                  int64_t k, int m, int out_fp32, void *stream);
+
+/* Y[i, r] = sum_j X[i, j] * W[r, j] for i < m (1..256 tokens, a prompt's
+ * prefill), r < n, j < k, on the tensor cores (tcgen05.mma, fp32
+ * accumulation in tensor memory, TMA-staged 128-byte-swizzled tiles). The
+ * projections that consume a decoded layer for many tokens: replaces, for
+ * these shapes, the nn.Linear the reference calls on decoded weights
+ * (afterimage/runtime/streaming_engine.py:1871-1915). W row-major [n, k] with
+ * row stride ldw, X [m, k] with row stride ldx (BF16, 16-byte aligned, row
+ * strides multiples of 8, k a multiple of 64); Y [m, n] BF16 with row stride
+ * ldy. When the 128-row tiles of W are too few to fill the GPU the K range is
+ * split: then `workspace` must hold aib_gemm_bf16_tc_workspace_floats(m, n, k)
+ * floats (0 when no split is needed). A bounded wait that gives up sets
+ * AIB_STATUS_WAIT_TIMEOUT in *d_status. Work is enqueued on `stream`. */
+int aib_gemm_bf16_tc(const void *w, int64_t ldw, const void *x, int64_t ldx, void *y, int64_t ldy, int64_t m,
+                     int64_t n, int64_t k, float *workspace, int64_t workspace_floats, int32_t *d_status,
+                     void *stream);
+int64_t aib_gemm_bf16_tc_workspace_floats(int64_t m, int64_t n, int64_t k);
+
 /* Elementwise recombine of an already-decoded exponent field: replaces
  * recombine_exponent_and_sign_mantissa / _recombine
  * (afterimage/runtime/compressed_store.py:94-130). */

@@ -10,9 +10,9 @@ a store by this package, and decoded by both of its decoders:
     above twice the cross-device bound below (all four steps here);
   * logits must equal transformers run on the same GPU -- the reference's
     forward is transformers -- bit for bit for the transformers-driven
-    engine and for the tensor-parallel decoder's unfused torch math; its
-    fused single-token kernels stay within FUSED_STEP_ATOL (bf16tol.py says
-    why);
+    engine and for the tensor-parallel decoder's unfused mode; its fused
+    mode (single-token kernels, own GEMV and tensor-core GEMM for the wide
+    projections) stays within FUSED_STEP_ATOL (bf16tol.py says why);
   * against the reference's CPU logits they must be within XDEV: transformers'
     own GPU forward differs from its CPU forward by up to 0.051 on these
     inputs (BF16 GEMMs of a different library round differently), so no
@@ -126,8 +126,13 @@ def test_tp_decoder_tokens_and_logits_match_the_reference(setup, golden, residen
         tokens.append(int(lg.argmax()))
         step = torch.tensor([[tokens[-1]]])
     logits = torch.stack(rec)
-    # step 0 is the prompt pass (the torch layer math in every mode)
-    assert torch.equal(logits[0], setup["hf_logits"][0])
+    # step 0 is the prompt pass: the torch layer math in every mode, with the wide
+    # projections (the head here) on this package's tensor-core GEMM in the fused mode
+    if dec.fused:
+        r = check_logits(logits[0], setup["hf_logits"][0], atol=FUSED_STEP_ATOL)
+        print("TP decoder %s %s prompt: max |logit - transformers on this GPU| %.4f" % (resident, kw, r["max_abs"]))
+    else:
+        assert torch.equal(logits[0], setup["hf_logits"][0])
     for t in range(1, setup["N"]):
         r = check_logits(logits[t], setup["hf_logits"][t], atol=FUSED_STEP_ATOL if dec.fused else 1e-2)
         print("TP decoder %s %s step %d: max |logit - transformers on this GPU| %.4f"
