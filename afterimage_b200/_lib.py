@@ -57,6 +57,7 @@ class StreamDesc(ctypes.Structure):
         ("elem_end", I64),
         ("sign_mantissa", P),
         ("out", P),
+        ("stripe_base", P),
     ]
 
 
@@ -94,6 +95,9 @@ SIGNATURES = [
     ("aib_decode_gemv_bf16_batch", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
     ("aib_decode_gemv_bf16_batch_noalloc", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
     ("aib_recombine", CI, [P, P, I64, P, P]),
+    ("aib_stripe_layout", CI, [P, I64, P, P]),
+    ("aib_stripe_stream", CI, [P, I64, I64, P, P, I64, I64, P, P, I64, P, P]),
+    ("aib_stripe_stream_host", CI, [P, I64, I64, P, P, I64, P, P, I64]),
     ("aib_selftest_wait_timeout", CI, [ctypes.c_uint, P, P]),
     ("aib_add_rmsnorm_bf16", CI, [P, P, P, P, I64, I64, ctypes.c_float, P]),
     ("aib_qk_rope_cache_bf16", CI, [P, CI, CI, CI, CI, P, P, ctypes.c_float, P, P, P, P, P, I64, P]),
@@ -124,7 +128,7 @@ def load():
                 fn = getattr(L, name)
                 fn.restype = res
                 fn.argtypes = args
-            if L.aib_abi_version() != 1:
+            if L.aib_abi_version() != 2:
                 raise AibError("libafterimage_b200.so ABI version mismatch")
             _lib = L
     return _lib

@@ -115,6 +115,7 @@ struct Job {
   int64_t offset_base;
   const int32_t *offs;    // entry c - chunk_base describes chunk c
   const int32_t *nbytes;
+  const int64_t *stripe;  // striped layout: first block of group g at entry g - chunk_base / 32; else null
   int64_t chunk_base;
   const uint2 *fast;
   const int32_t *flags;
@@ -410,6 +411,7 @@ struct Window {
   int pos;   // bits consumed, counted from the first byte of block b0 (the block of the chunk's first byte)
   int lo;    // the lowest block (relative to b0) the window may still read
   int end;   // bit index of the chunk's end, same origin as pos
+  int sh;    // the chunk's j-th block is block b0 + (j << sh): 0 in the reference layout, 5 striped
   int64_t b0;
 };
 
@@ -418,7 +420,7 @@ struct Window {
 __device__ __forceinline__ void win_request(const Window &r, int j, unsigned char *ring, const uint4 *src,
                                             int64_t bmax, uint64_t pol) {
   const int slot = j & (kSlots - 1);
-  const uint4 *g = src + min(r.b0 + j, bmax);
+  const uint4 *g = src + min(r.b0 + (static_cast<int64_t>(j) << r.sh), bmax);
   asm volatile("cp.async.cg.shared.global.L2::cache_hint.L2::256B [%0], [%1], 16, 16, %2;" ::"r"(
                    smem_u32(ring + slot * 16)),
                "l"(g), "l"(pol)
@@ -429,9 +431,12 @@ __device__ __forceinline__ void win_request(const Window &r, int j, unsigned cha
   asm volatile("cp.async.commit_group;" ::: "memory");
 }
 
+// pos: the chunk's first byte (reference layout: its byte offset; striped:
+// 16 x its first block). sh: log2 of the block stride.
 __device__ __forceinline__ void win_init(Window &r, unsigned char *ring, const uint4 *src, int64_t bmax,
-                                         int64_t pos, int64_t nbytes, uint64_t pol) {
+                                         int64_t pos, int64_t nbytes, int sh, uint64_t pol) {
   r.b0 = pos >> 4;
+  r.sh = sh;
   r.pos = static_cast<int>(pos & 15) * 8;
   r.lo = 0;
   r.end = static_cast<int>(min(static_cast<int64_t>(r.pos) + nbytes * 8, static_cast<int64_t>(INT32_MAX)));
@@ -523,16 +528,27 @@ __device__ __forceinline__ void decode_groups(const Job &J, const uint2 *s_fast,
     const int need = active ? static_cast<int>(min(cs, J.e1 - c * cs)) : 0;
 
     Window rd;
-    rd.pos = 0; rd.lo = 0; rd.end = 0; rd.b0 = 0;
+    rd.pos = 0; rd.lo = 0; rd.end = 0; rd.sh = 0; rd.b0 = 0;
     if (active) {
-      int64_t pos = static_cast<int64_t>(J.offs[c - J.chunk_base]) - J.offset_base;
       int64_t nbyt = J.nbytes[c - J.chunk_base];
-      if (pos < 0 || nbyt < 0 || pos + nbyt > J.packed_nbytes) {
+      int64_t pos;
+      bool bad;
+      if (J.stripe) {
+        // block i of the chunk: stripe_base[group] + (c mod 32) + 32 i
+        const int64_t sb = J.stripe[(c >> 5) - (J.chunk_base >> 5)];
+        bad = sb < 0 || sb > J.packed_nbytes / 16 || nbyt < 0;
+        pos = bad ? 0 : (sb + (c & 31)) * 16;
+        bad = bad || (nbyt > 0 && pos + ((nbyt - 1) >> 4) * 512 + 16 > J.packed_nbytes);
+      } else {
+        pos = static_cast<int64_t>(J.offs[c - J.chunk_base]) - J.offset_base;
+        bad = pos < 0 || nbyt < 0 || pos + nbyt > J.packed_nbytes;
+      }
+      if (bad) {
         if (status) atomicOr(status, AIB_STATUS_BAD_CHUNK_RANGE);
         pos = 0;
         nbyt = 0;
       }
-      win_init(rd, my_stream, src, bmax, pos, nbyt, pol_keep);
+      win_init(rd, my_stream, src, bmax, pos, nbyt, J.stripe ? 5 : 0, pol_keep);
     }
 
     const int max_need = fast ? static_cast<int>(cs)
@@ -1047,8 +1063,12 @@ static int make_job(const aib_stream_desc *d, int mode, Job *j, bool *empty) {
     return aib_set_errorf("packed_capacity %lld must be a multiple of 16, >= 16 and >= packed_nbytes %lld",
                           (long long)d->packed_capacity, (long long)d->packed_nbytes),
            AIB_EINVAL;
-  if (!d->chunk_offsets || !d->chunk_nbytes || !d->tables || !d->sym_lut || !d->len_lut || !d->out)
+  if ((!d->chunk_offsets && !d->stripe_base) || !d->chunk_nbytes || !d->tables || !d->sym_lut || !d->len_lut ||
+      !d->out)
     return aib_set_error("null device pointer in descriptor"), AIB_EINVAL;
+  if (d->stripe_base && d->chunk_base % 32)
+    return aib_set_errorf("a striped stream's chunk_base must be a multiple of 32, got %lld", (long long)d->chunk_base),
+           AIB_EINVAL;
   if (!aligned(d->tables, 16)) return aib_set_error("tables must be 16-byte aligned"), AIB_EINVAL;
   if (mode == kModeBF16 && !d->sign_mantissa) return aib_set_error("sign_mantissa is required"), AIB_EINVAL;
   if (!aligned(d->out, mode == kModeBF16 ? 2 : (mode == kModeI32 ? 4 : 1)))
@@ -1060,6 +1080,7 @@ static int make_job(const aib_stream_desc *d, int mode, Job *j, bool *empty) {
   j->offset_base = d->offset_base;
   j->offs = d->chunk_offsets;
   j->nbytes = d->chunk_nbytes;
+  j->stripe = d->stripe_base;
   j->chunk_base = d->chunk_base;
   j->fast = static_cast<const uint2 *>(d->tables);
   j->flags = reinterpret_cast<const int32_t *>(static_cast<const unsigned char *>(d->tables) + kFastBytes);
@@ -1175,6 +1196,7 @@ static int gemv_launch(const aib_gemv_desc *descs, int count, int32_t *status, v
       return aib_set_error("gemv: the element range must be whole rows"), AIB_EINVAL;
     if (!d.sign_mantissa || !aligned(d.sign_mantissa, 4))
       return aib_set_error("gemv: sign_mantissa must be a 4-byte aligned device pointer"), AIB_EINVAL;
+    if (d.stripe_base) return aib_set_error("gemv: the stream must be in the reference layout (stripe_base NULL)"), AIB_EINVAL;
     // the stream checks shared with the decode (out is not written here)
     aib_stream_desc copy = d;
     copy.out = g->y;
@@ -1253,7 +1275,7 @@ static int gemv_launch(const aib_gemv_desc *descs, int count, int32_t *status, v
 using namespace aib;
 
 AIB_API const char *aib_last_error(void) { return g_err; }
-AIB_API int aib_abi_version(void) { return 1; }
+AIB_API int aib_abi_version(void) { return 2; }
 AIB_API size_t aib_tables_bytes(void) { return kTablesBytes; }
 
 AIB_API int aib_build_tables(const int32_t *d_sym_lut, const int8_t *d_len_lut, int max_bits, void *d_tables,

@@ -98,6 +98,13 @@ class DeviceStream:
     offsets: torch.Tensor
     chunk_nbytes: torch.Tensor
     chunk_base: int
+    # striped layout (aib_stripe_stream): each group's first 16-byte block;
+    # None for the reference layout
+    stripe_base: torch.Tensor | None = None
+
+    @property
+    def striped(self) -> bool:
+        return self.stripe_base is not None
 
 
 def upload_stream(enc, dev: torch.device, c0: int = 0, c1: int | None = None) -> DeviceStream:
@@ -123,6 +130,62 @@ def upload_stream(enc, dev: torch.device, c0: int = 0, c1: int | None = None) ->
                         chunk_nbytes=upload(nbs[c0:c1], dev, np.int32), chunk_base=c0)
 
 
+def stripe_layout(chunk_nbytes: np.ndarray) -> np.ndarray:
+    """int64[ceil(n / 32) + 1]: each chunk group's first block in the striped
+    layout, then the total (aib_stripe_layout)."""
+    nbs = np.ascontiguousarray(chunk_nbytes, dtype=np.int32)
+    n = int(nbs.shape[0])
+    base = np.zeros((n + 31) // 32 + 1, dtype=np.int64)
+    total = ctypes.c_int64(0)
+    _lib.check(_lib.load().aib_stripe_layout(nbs.ctypes.data if n else None, n, base.ctypes.data,
+                                             ctypes.byref(total)), "stripe_layout")
+    return base
+
+
+def stripe_host(packed: np.ndarray, chunk_offsets: np.ndarray, chunk_nbytes: np.ndarray,
+                offset_base: int = 0) -> tuple[np.ndarray, np.ndarray]:
+    """(striped bytes, group_base) of a reference-layout stream, made on the
+    host (aib_stripe_stream_host) for images that are built on the host."""
+    src = np.ascontiguousarray(packed, dtype=np.uint8)
+    offs = np.ascontiguousarray(chunk_offsets, dtype=np.int32)
+    nbs = np.ascontiguousarray(chunk_nbytes, dtype=np.int32)
+    base = stripe_layout(nbs)
+    out = np.zeros(max(16, int(base[-1]) * 16), dtype=np.uint8)
+    if nbs.shape[0]:
+        _lib.check(_lib.load().aib_stripe_stream_host(
+            src.ctypes.data, src.shape[0], int(offset_base), offs.ctypes.data, nbs.ctypes.data, nbs.shape[0],
+            base.ctypes.data, out.ctypes.data, out.shape[0]), "stripe_stream_host")
+    return out[:int(base[-1]) * 16], base
+
+
+def stripe_stream(ds: DeviceStream, chunk_nbytes: np.ndarray, dev: torch.device) -> DeviceStream:
+    """The striped copy of a reference-layout device stream (chunk_base a
+    multiple of 32). `chunk_nbytes` is the host copy of ds.chunk_nbytes'
+    entries. Stream-ordered on the current stream; ds.packed can be dropped
+    once this is enqueued (the caching allocator reuses it in stream order)."""
+    if ds.striped:
+        return ds
+    if ds.chunk_base % 32:
+        raise ValueError(f"striping needs a chunk range starting at a multiple of 32, got {ds.chunk_base}")
+    nbs = np.ascontiguousarray(chunk_nbytes, dtype=np.int32)
+    n = int(nbs.shape[0])
+    base = stripe_layout(nbs)
+    total = int(base[-1]) * 16
+    cap = max(16, total)
+    # the kernel writes every block of every group region; a stream with no
+    # blocks keeps its one (never read) block zeroed
+    dst = torch.empty(cap, dtype=torch.uint8, device=dev) if total else torch.zeros(cap, dtype=torch.uint8,
+                                                                                     device=dev)
+    d_base = torch.from_numpy(base).to(dev)
+    if n:
+        _lib.check(_lib.load().aib_stripe_stream(
+            ds.packed.data_ptr(), ds.nbytes, ds.offset_base, ds.offsets.data_ptr(), ds.chunk_nbytes.data_ptr(),
+            ds.chunk_base, n, d_base.data_ptr(), dst.data_ptr(), cap, status_word(dev).data_ptr(),
+            stream_ptr(dev)), "stripe_stream")
+    return DeviceStream(packed=dst, nbytes=total, capacity=cap, offset_base=0, offsets=ds.offsets,
+                        chunk_nbytes=ds.chunk_nbytes, chunk_base=ds.chunk_base, stripe_base=d_base)
+
+
 def make_desc(ds: DeviceStream, tables, enc, e0: int, e1: int, out: torch.Tensor,
               sign_mantissa: torch.Tensor | None = None) -> _lib.StreamDesc:
     d = _lib.StreamDesc()
@@ -143,6 +206,7 @@ def make_desc(ds: DeviceStream, tables, enc, e0: int, e1: int, out: torch.Tensor
     d.elem_end = int(e1)
     d.sign_mantissa = sign_mantissa.data_ptr() if sign_mantissa is not None else None
     d.out = out.data_ptr()
+    d.stripe_base = ds.stripe_base.data_ptr() if ds.stripe_base is not None else None
     return d
 
 

@@ -804,6 +804,9 @@ def main(argv=None) -> int:
     ap.add_argument("--workload", default="qwen3-14b-layer", choices=sorted(WORKLOADS))
     ap.add_argument("--layers", type=int, default=2, help="distinct resident layers used round-robin")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--layout", default="striped", choices=["striped", "reference"],
+                    help="device layout of the resident streams: striped (aib_stripe_stream, coalesced "
+                         "stream copies) or the reference's back-to-back chunks")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--tokens", action="store_true",
@@ -845,7 +848,10 @@ def main(argv=None) -> int:
     host_layers = [h for h, _ in made]
     sources = [s for _, s in made]  # BF16 source of every resident layer, on the device
     del made
-    resident = [[LD.upload_layer(t, dev) for t in layer] for layer in host_layers]
+    resident = [[LD.upload_layer(t, dev, striped=args.layout == "striped") for t in layer]
+                for layer in host_layers]
+    stream_bytes = sum(int(np.asarray(t.encoded.packed).nbytes) for t in host_layers[0])
+    resident_stream_bytes = sum(r.stream.nbytes for r in resident[0])
     outs = [torch.empty(r, c, dtype=torch.bfloat16, device=dev) for _, r, c in spec]
     decoder = LD.LayerDecoder(dev)
     descs = [decoder.descriptors(res, outs) for res in resident]
@@ -954,6 +960,8 @@ def main(argv=None) -> int:
                          "frac": round(achieved / peak, 4), "peak_source": peak_src,
                          "traffic": profile_traffic(args.workload),
                          "kernel": "aib::decode_kernel<0> (fused decode + recombine)",
+                         "stream_layout": args.layout,
+                         "resident_stream_bytes_vs_reference": round(resident_stream_bytes / stream_bytes, 4),
                          "avg_launch_ms": round(avg_launch_ms, 5)},
             "parity": parity,
             "clocks": clocks,

@@ -137,7 +137,51 @@ typedef struct aib_stream_desc {
   int64_t elem_end;             /* one past the last element (<= n_symbols) */
   const uint8_t *sign_mantissa; /* device; element elem_begin at index 0 (bf16 decode only) */
   void *out;                    /* device; element elem_begin at index 0 */
+  const int64_t *stripe_base;   /* NULL: `packed` holds the reference stream (chunk c at
+                                   packed + chunk_offsets[c - chunk_base] - offset_base).
+                                   Non-NULL: `packed` holds the striped layout that
+                                   aib_stripe_stream writes and entry g - chunk_base / 32 is
+                                   the first 16-byte block of chunk group g; chunk_base is then
+                                   a multiple of 32, chunk_offsets and offset_base are unused
+                                   and packed_nbytes is the striped size. */
 } aib_stream_desc;
+
+/* Striped resident layout (no counterpart in the reference, which reads
+ * each chunk's bytes where the encoder put them). Chunks are taken in groups
+ * of 32 (group g = chunks 32g .. 32g + 31); in a group's region the 16-byte
+ * block i of the chunk in column l (= c mod 32) is block i * 32 + l, so the
+ * 32 lanes of a decoding warp, one chunk each, read 512 consecutive bytes per
+ * step instead of 32 scattered 16-byte blocks. A group's region has as many
+ * rows as its longest chunk has blocks; blocks past a chunk's end are zero.
+ * The stream is the same bits; only the bytes' places differ.
+ *
+ * aib_stripe_layout (host): from the chunks' byte counts (host int32[n_chunks])
+ * writes group_base[g] = the region's first block for g in
+ * [0, ceil(n_chunks / 32)] (the last entry is the total) and returns that
+ * total in *total_blocks. */
+int aib_stripe_layout(const int32_t *chunk_nbytes, int64_t n_chunks, int64_t *group_base, int64_t *total_blocks);
+/* aib_stripe_stream (device, stream-ordered): writes the striped copy of the
+ * reference stream `src` (chunks [chunk_base, chunk_base + n_chunks) described
+ * as in aib_stream_desc; chunk_base a multiple of 32) into dst (16-byte
+ * aligned, dst_nbytes >= 16 * group_base[last], a multiple of 16). group_base
+ * is the device copy of aib_stripe_layout's array. A chunk whose bytes lie
+ * outside src_nbytes, or a group region outside dst, sets
+ * AIB_STATUS_BAD_CHUNK_RANGE in d_status (optional); such a chunk is written
+ * as zeros and such a region not at all. */
+int aib_stripe_stream(const uint8_t *src, int64_t src_nbytes, int64_t offset_base, const int32_t *chunk_offsets,
+                      const int32_t *chunk_nbytes, int64_t chunk_base, int64_t n_chunks,
+                      const int64_t *group_base, uint8_t *dst, int64_t dst_nbytes, int32_t *d_status,
+                      void *stream);
+
+/* aib_stripe_stream_host: the same striped copy made on the host (for
+ * images that are built on the host and copied whole), chunk c of the
+ * arrays at src + chunk_offsets[c] - offset_base. Returns AIB_EINVAL when
+ * dst is smaller than 16 * group_base[last] (nothing written), or at the
+ * first group with a bad region or a chunk that lies outside src or does
+ * not fit its region (dst then holds the groups before it). */
+int aib_stripe_stream_host(const uint8_t *src, int64_t src_nbytes, int64_t offset_base,
+                           const int32_t *chunk_offsets, const int32_t *chunk_nbytes, int64_t n_chunks,
+                           const int64_t *group_base, uint8_t *dst, int64_t dst_nbytes);
 
 /* Fused decode + recombine: out (uint16 bf16 bits) = the reference's
  * decompress output for elements [elem_begin, elem_end). Replaces the
@@ -167,7 +211,8 @@ int aib_decode_bf16_batch(const aib_stream_desc *descs, int count, int32_t *d_st
  * row-major [rows, cols] matrix (elem_begin and elem_end multiples of
  * cols), cols a multiple of chunk_size, chunk_size a multiple of 4,
  * sign_mantissa 4-byte aligned;
- * stream.out is ignored. Replaces, for M = 1, the decode followed by the
+ * stream.out is ignored and stream.stripe_base must be NULL (its lanes
+ * read chunks a row apart, not 32 neighbours). Replaces, for M = 1, the decode followed by the
  * consuming nn.Linear / F.linear on the decoded weights
  * (afterimage/runtime/streaming_engine.py:1871-1915 layer hooks around the
  * transformers decoder layer; the chunked head's F.linear, :2330). */

@@ -122,7 +122,7 @@ def test_gemv_host_validation_without_a_gpu():
 
 def test_tables_bytes_and_abi_version():
     L = _lib.load()
-    assert L.aib_abi_version() == 1
+    assert L.aib_abi_version() == 2
     assert L.aib_tables_bytes() % 16 == 0 and L.aib_tables_bytes() >= 4096 * 8
 
 

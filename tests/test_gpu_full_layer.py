@@ -1,7 +1,8 @@
 """GPU parity at the benchmark's full size: one Qwen3-14B-shaped decoder
 layer (q/k/v/o/gate/up/down, 330.3 M BF16 weights) decoded by ONE batched
 launch (aib_decode_bf16_batch, 7 tensors, ~2.9 waves of CTAs), in the three
-chunkings the benchmark and the tensor-parallel stores use:
+chunkings the benchmark and the tensor-parallel stores use, with the
+stream in the reference layout and in the striped device layout:
   * the reference's default, 1024 symbols for every tensor;
   * TP-ready (whole chunks per rank up to TP 8): o_proj 640, down_proj 1088;
   * the TP-8 store: 256, with o_proj 320 and down_proj 128.
@@ -32,15 +33,16 @@ def weights():
     return [(name, (torch.randn(r, c, generator=g) * 0.02).to(torch.bfloat16)) for name, r, c in LAYER]
 
 
+@pytest.mark.parametrize("layout", ["reference", "striped"])
 @pytest.mark.parametrize("chunking", sorted(CHUNKINGS))
-def test_full_14b_layer_one_launch_is_bit_exact(weights, chunking):
+def test_full_14b_layer_one_launch_is_bit_exact(weights, chunking, layout):
     from afterimage_b200.runtime import _device
     from afterimage_b200.runtime.compressed_store import compress_layer
     from afterimage_b200.runtime.layer_decode import LayerDecoder, upload_layer
     dev = torch.device("cuda", 0)
     sizes = CHUNKINGS[chunking]
     layers = [compress_layer(W, chunk_size=sizes.get(name, sizes.get("*", 1024))) for name, W in weights]
-    resident = [upload_layer(layer, dev) for layer in layers]
+    resident = [upload_layer(layer, dev, striped=layout == "striped") for layer in layers]
     outs = [torch.full(W.shape, float("nan"), dtype=torch.bfloat16, device=dev) for _, W in weights]
     dec = LayerDecoder(dev)
     descs = dec.descriptors(resident, outs)
