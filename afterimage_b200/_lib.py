@@ -29,6 +29,7 @@ STATUS_BAD_CHUNK_RANGE = 1
 STATUS_LUT_NOT_PREFIX = 2
 STATUS_LUT_RANGE = 4
 STATUS_WAIT_TIMEOUT = 8
+STATUS_PEER_TIMEOUT = 16
 WAIT_LIMIT_POLLS = 1 << 22  # AIB_WAIT_LIMIT_POLLS
 
 P = ctypes.c_void_p
@@ -72,6 +73,21 @@ class GemvDesc(ctypes.Structure):
     ]
 
 
+AR_MAX_RANKS = 8      # AIB_AR_MAX_RANKS
+AR_MAX_CTAS = 64      # AIB_AR_MAX_CTAS
+AR_HANDLE_BYTES = 64  # AIB_AR_HANDLE_BYTES
+
+
+class ArGroup(ctypes.Structure):
+    """aib_ar_group (include/afterimage_b200.h)."""
+    _fields_ = [
+        ("buffers", P * AR_MAX_RANKS),
+        ("rank", I32),
+        ("world", I32),
+        ("max_floats", I64),
+    ]
+
+
 # (name, restype, argtypes) of every exported entry point; tests check that
 # the header declares exactly these.
 SIGNATURES = [
@@ -98,6 +114,14 @@ SIGNATURES = [
     ("aib_stripe_layout", CI, [P, I64, P, P]),
     ("aib_stripe_stream", CI, [P, I64, I64, P, P, I64, I64, P, P, I64, P, P]),
     ("aib_stripe_stream_host", CI, [P, I64, I64, P, P, I64, P, P, I64]),
+    ("aib_ar_buffer_bytes", ctypes.c_size_t, [I64]),
+    ("aib_ar_alloc", CI, [I64, P]),
+    ("aib_ar_free", CI, [P]),
+    ("aib_ar_ipc_handle", CI, [P, P]),
+    ("aib_ar_ipc_open", CI, [P, P]),
+    ("aib_ar_ipc_close", CI, [P]),
+    ("aib_ar_ctas", CI, [I64]),
+    ("aib_allreduce_oneshot_f32", CI, [P, P, P, I64, ctypes.c_uint, P, P]),
     ("aib_selftest_wait_timeout", CI, [ctypes.c_uint, P, P]),
     ("aib_add_rmsnorm_bf16", CI, [P, P, P, P, I64, I64, ctypes.c_float, P]),
     ("aib_qk_rope_cache_bf16", CI, [P, CI, CI, CI, CI, P, P, ctypes.c_float, P, P, P, P, P, I64, P]),

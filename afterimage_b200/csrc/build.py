@@ -24,7 +24,7 @@ INCLUDE = ROOT / "include"
 LIBDIR = PKG / "lib"
 LIB = LIBDIR / "libafterimage_b200.so"
 
-CU_SOURCES = ["decode.cu", "tp_ops.cu", "gemv.cu", "gemm_tc.cu", "stripe.cu"]
+CU_SOURCES = ["decode.cu", "tp_ops.cu", "gemv.cu", "gemm_tc.cu", "stripe.cu", "allreduce.cu"]
 CPP_SOURCES = ["encode.cpp", "io.cpp"]
 HEADERS = ["aib_internal.h"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]

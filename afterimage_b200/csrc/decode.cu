@@ -96,7 +96,12 @@ constexpr int kTablesBytes = kFastBytes + 16;  // fast table + {flags, max_bits,
 constexpr int kWarps = AIB_WARPS;
 constexpr int kThreads = kWarps * 32;
 constexpr int kPhase = AIB_PHASE;  // symbols per lane between merges (multiple of 32)
-constexpr int kRing = kPhase * 2;  // ring bytes per lane (power of two >= kPhase + 11)
+#ifndef AIB_RING_MULT
+#define AIB_RING_MULT 2
+#endif
+// ring bytes per lane (a power of two >= kPhase + 4 * kLookups + 4); what
+// exceeds kPhase is the slack a lane may decode ahead of its warp's merge
+constexpr int kRing = kPhase * AIB_RING_MULT;
 constexpr int kRow = kRing + 8;   // padded row: lanes at equal k hit different banks
 constexpr int kRingWarpBytes = 32 * kRow;
 constexpr int kSlots = AIB_SLOTS;                // stream ring slots per lane (power of two >= 2)
@@ -406,6 +411,7 @@ constexpr int kLookups = AIB_LOOKUPS;
 // bits) after kLookups - 1 of them
 static_assert(kLookups * kFastBits <= 64 && (kLookups - 1) * kFastBits + 16 <= 64, "a window holds 64 bits");
 static_assert(kSlots >= 4, "the window needs the current and the next block, two more in flight");
+static_assert((kRing & (kRing - 1)) == 0 && kRing >= kPhase + 4 * kLookups + 4, "ring: a power of two with slack");
 
 struct Window {
   int pos;   // bits consumed, counted from the first byte of block b0 (the block of the chunk's first byte)
@@ -1113,6 +1119,37 @@ static int make_job(const aib_stream_desc *d, int mode, Job *j, bool *empty) {
 
 // groups of 32 chunks handled per warp before a CTA is considered full
 static constexpr int kGroupsPerWarp = 1;
+#ifndef AIB_WAVES
+#define AIB_WAVES 4
+#endif
+// most CTAs a launch uses, in waves of (SMs x resident CTAs per SM)
+static constexpr int kMaxWaves = AIB_WAVES;
+
+// Splits `cap` CTAs over n jobs in proportion to their groups by largest
+// remainder, each job at least 1 CTA and at most max_useful[i]. The shares
+// add up to cap unless the per-job bounds force otherwise, so a launch
+// sized to whole waves does not spill a few CTAs into one more wave.
+static void apportion(int64_t cap, const int64_t *groups, const int64_t *max_useful, int n, int64_t total,
+                      int32_t *share) {
+  int64_t sum = 0;
+  int64_t rem[AIB_MAX_BATCH];  // cap * groups - share * total: what the job is still owed
+  for (int i = 0; i < n; ++i) {
+    const int64_t q = cap * groups[i];
+    const int64_t s = std::max<int64_t>(1, std::min(q / total, max_useful[i]));
+    rem[i] = q - s * total;
+    share[i] = static_cast<int32_t>(s);
+    sum += s;
+  }
+  while (sum < cap) {
+    int best = -1;
+    for (int i = 0; i < n; ++i)
+      if (share[i] < max_useful[i] && (best < 0 || rem[i] > rem[best])) best = i;
+    if (best < 0) break;
+    ++share[best];
+    rem[best] -= total;
+    ++sum;
+  }
+}
 
 template <int MODE>
 static int launch(const aib_stream_desc *descs, int count, int32_t *status, void *stream) {
@@ -1145,16 +1182,19 @@ static int launch(const aib_stream_desc *descs, int count, int32_t *status, void
   const int64_t wave = static_cast<int64_t>(di->sms) * di->occ[MODE];
   int64_t want = (total_groups + kWarps * kGroupsPerWarp - 1) / (kWarps * kGroupsPerWarp);
   if (AIB_SPREAD) want = std::max(want, std::min(total_groups, wave));
-  const int64_t cap = std::max<int64_t>(want, 1) < 4 * wave ? std::max<int64_t>(want, 1) : 4 * wave;
+  const int64_t cap = std::min<int64_t>(std::max<int64_t>(want, 1), kMaxWaves * wave);
+  int64_t groups[AIB_MAX_BATCH], max_useful[AIB_MAX_BATCH];
+  int32_t share[AIB_MAX_BATCH];
+  for (int i = 0; i < n; ++i) {
+    groups[i] = batch.job[i].n_groups;
+    max_useful[i] = AIB_SPREAD ? groups[i] : (groups[i] + kWarps - 1) / kWarps;
+  }
+  apportion(cap, groups, max_useful, n, total_groups, share);
   int cta = 0;
   for (int i = 0; i < n; ++i) {
-    Job &j = batch.job[i];
-    int64_t share = (cap * j.n_groups + total_groups - 1) / total_groups;
-    const int64_t max_useful = AIB_SPREAD ? j.n_groups : (j.n_groups + kWarps - 1) / kWarps;
-    share = std::max<int64_t>(1, std::min(share, max_useful));
-    j.cta_begin = cta;
-    j.ctas = static_cast<int32_t>(share);
-    cta += j.ctas;
+    batch.job[i].cta_begin = cta;
+    batch.job[i].ctas = share[i];
+    cta += share[i];
   }
   int n_default = 0;
   for (int i = 0; i < n; ++i) n_default += batch.job[i].chunk_size == kDefaultChunk;
@@ -1241,15 +1281,20 @@ static int gemv_launch(const aib_gemv_desc *descs, int count, int32_t *status, v
   const int64_t wave = static_cast<int64_t>(di->sms) * di->gemv_occ;
   int64_t want = std::max<int64_t>(1, (total_groups + kWarps - 1) / kWarps);
   if (AIB_SPREAD) want = std::max(want, std::min(total_groups, wave));
-  const int64_t cap = std::min<int64_t>(want, 4 * wave);
+  const int64_t cap = std::min<int64_t>(want, kMaxWaves * wave);
+  int64_t groups[AIB_MAX_BATCH], max_useful[AIB_MAX_BATCH];
+  int32_t share[AIB_MAX_BATCH];
+  for (int i = 0; i < n; ++i) {
+    groups[i] = batch.job[i].n_groups;
+    max_useful[i] = AIB_SPREAD ? groups[i] : (groups[i] + kWarps - 1) / kWarps;
+  }
+  apportion(cap, groups, max_useful, n, total_groups, share);
   int cta = 0;
   int n_default = 0;
   for (int i = 0; i < n; ++i) {
     GemvJob &G = batch.job[i];
-    int64_t share = (cap * G.n_groups + total_groups - 1) / total_groups;
-    share = std::max<int64_t>(1, std::min(share, AIB_SPREAD ? G.n_groups : (G.n_groups + kWarps - 1) / kWarps));
     G.cta_begin = cta;
-    G.ctas = static_cast<int32_t>(share);
+    G.ctas = share[i];
     cta += G.ctas;
     n_default += G.chunk_size == kDefaultChunk;
   }

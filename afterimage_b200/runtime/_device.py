@@ -63,7 +63,9 @@ def check_status(dev: torch.device) -> None:
             bits.append("a chunk's byte range lies outside the packed stream (corrupt offsets)")
         if v & _lib.STATUS_WAIT_TIMEOUT:
             bits.append("a bounded shared-memory copy wait timed out")
-        if v & ~(_lib.STATUS_BAD_CHUNK_RANGE | _lib.STATUS_WAIT_TIMEOUT):
+        if v & _lib.STATUS_PEER_TIMEOUT:
+            bits.append("a one-shot all-reduce gave up waiting for a peer rank")
+        if v & ~(_lib.STATUS_BAD_CHUNK_RANGE | _lib.STATUS_WAIT_TIMEOUT | _lib.STATUS_PEER_TIMEOUT):
             bits.append(f"status bits 0x{v:x}")
         raise RuntimeError("afterimage_b200 decode failed: " + "; ".join(bits))
 

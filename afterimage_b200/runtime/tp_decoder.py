@@ -271,6 +271,7 @@ class TPDecoder:
         self.w = weights  # key -> tensor (shard) or a callable returning it
         self.timeline = None  # a list to record (kind, layer, start event, end event) into
         self._graph_state = None
+        self.allreducer = None  # one-shot NVLink all-reduce (use_oneshot_allreduce); else NCCL
         rp = getattr(hf_cfg, "rope_parameters", None) or {}
         theta = rp.get("rope_theta", getattr(hf_cfg, "rope_theta", 10000.0))
         self.inv_freq = 1.0 / (theta ** (torch.arange(0, self.hd, 2, dtype=torch.int64).to(
@@ -330,6 +331,17 @@ class TPDecoder:
         return w() if callable(w) else w
 
     # -- collectives ----------------------------------------------------------
+    def use_oneshot_allreduce(self, max_floats: int = 1 << 20) -> None:
+        """Collective (every rank calls it): the row-parallel sums of up to
+        max_floats floats go through the one-shot NVLink all-reduce
+        (runtime/allreduce.py, csrc/allreduce.cu) instead of NCCL; larger
+        ones (long prompts) stay on NCCL. A CPU or single-rank decoder keeps
+        what it has."""
+        if self.world < 2 or self.device.type != "cuda" or self.allreducer is not None:
+            return
+        from .allreduce import OneShotAllReduce
+        self.allreducer = OneShotAllReduce(self.group, self.device, max_floats)
+
     def _all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
             torch.distributed.all_reduce(x, group=self.group)
@@ -373,7 +385,14 @@ class TPDecoder:
             y = torch.mm(x2, w.t(), out_dtype=torch.float32)
         else:
             y = x2.float() @ w.float().t()
-        torch.distributed.all_reduce(y, group=self.group)
+        t0 = _mark(torch.cuda.current_stream(self.device)) \
+            if self.timeline is not None and self.device.type == "cuda" else None
+        if self.allreducer is not None and y.numel() <= self.allreducer.max_floats:
+            self.allreducer(y)
+        else:
+            torch.distributed.all_reduce(y, group=self.group)
+        if t0 is not None:
+            self.timeline.append(("allreduce", -1, t0, _mark(torch.cuda.current_stream(self.device))))
         return y.to(x.dtype).reshape(*x.shape[:-1], w.shape[0])
 
     def _all_gather_last(self, x: torch.Tensor) -> torch.Tensor:
@@ -622,7 +641,11 @@ class TPDecoder:
         self._graph_state = None
 
     def close(self) -> None:
+        """Collective when the one-shot all-reduce is in use."""
         self.release_graphs()
+        if self.allreducer is not None:
+            self.allreducer.close()
+            self.allreducer = None
 
     def head_logits(self, x: torch.Tensor) -> torch.Tensor:
         """This rank's vocab shard of the logits."""
@@ -1157,7 +1180,10 @@ def load_tp_decoder(store_dir, hf_cfg, world: int = 1, rank: int = 0, group=None
                              copied to the device one layer at a time.
     Norms are replicated; the head is split by vocabulary (kept compressed
     unless decoded); an untied row-gather embedding stays in host memory
-    when streamed. Extra keywords go to CompressedTPDecoder."""
+    when streamed. collective="oneshot" (default) sums the row-parallel
+    projections with the one-shot NVLink all-reduce on GPU ranks (NCCL
+    otherwise, and for sums above its buffer); "nccl" keeps NCCL. Extra
+    keywords go to CompressedTPDecoder."""
     from .compressed_store import decompress_layer_gpu
     if resident not in ("decoded", "compressed", "streamed"):
         raise ValueError("resident must be 'decoded', 'compressed' or 'streamed'")
@@ -1203,7 +1229,14 @@ def load_tp_decoder(store_dir, hf_cfg, world: int = 1, rank: int = 0, group=None
             weights[key] = ss.finish(decompress_layer_gpu(ss.layer, device=dev))
     if "lm_head.weight" not in weights and not getattr(hf_cfg, "tie_word_embeddings", False):
         raise RuntimeError("store has no lm_head.weight and the model is not tied")
+    collective = kw.pop("collective", "oneshot")
+    if collective not in ("oneshot", "nccl"):
+        raise ValueError("collective must be 'oneshot' or 'nccl'")
     if keep_compressed:
-        return CompressedTPDecoder(hf_cfg, weights, streams, world, rank, group, dev,
-                                   mode="streamed" if resident == "streamed" else "compressed", **kw)
-    return TPDecoder(hf_cfg, weights, world, rank, group, dev, fused=kw.get("fused", True))
+        dec = CompressedTPDecoder(hf_cfg, weights, streams, world, rank, group, dev,
+                                  mode="streamed" if resident == "streamed" else "compressed", **kw)
+    else:
+        dec = TPDecoder(hf_cfg, weights, world, rank, group, dev, fused=kw.get("fused", True))
+    if collective == "oneshot":
+        dec.use_oneshot_allreduce()
+    return dec

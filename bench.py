@@ -80,9 +80,8 @@ MODELS = {
     "mistral-24b": ("MistralConfig", MISTRAL_24B, 256, 4, 8.0, "Mistral-Small-24B shape"),
 }
 METRIC = "bit-exact BF16 weight decode GB/s"
-# host -> device copy rate of one B200 (PCIe 5 x16) measured on this pool: pinned copies of
-# hundreds of MB reach 55 GB/s (bench timelines, "h2d_gbps_in_step")
-PCIE_GBS = 55.0
+# host -> device copy rate assumed only when link_rates() cannot measure it (no CUDA)
+PCIE_GBS_FALLBACK = 55.0
 
 
 def env_int(name, default):
@@ -410,31 +409,81 @@ def _barrier(world: int) -> None:
         torch.distributed.barrier()
 
 
-def allreduce_probe(world: int, dev, hidden: int, count: int) -> dict | None:
+def link_rates(world: int, rank: int, dev, nbytes: int = 1 << 30) -> dict:
+    """Measured link rates on this box, CUDA events, max time over ranks:
+      pcie_h2d_gbps / pcie_d2h_gbps: one pinned 1 GiB copy per rank, every
+        rank at once (as the streamed decoder's ranks copy), per-rank rate;
+      nvlink_p2p_gbps (world >= 2): rank 0 sends 1 GiB to rank 1 over NCCL's
+        peer-to-peer path (NVLink through NVSwitch), one direction."""
+    host = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    buf = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    out = {}
+    for name, dst, src in (("pcie_h2d_gbps", buf, host), ("pcie_d2h_gbps", host, buf)):
+        dst.copy_(src, non_blocking=True)  # warm
+        torch.cuda.synchronize()
+        _barrier(world)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        ms = _max_over_ranks(a.elapsed_time(b), world, dev)
+        out[name] = round(nbytes / (ms / 1e3) / 1e9, 2)
+    del host
+    if world >= 2:
+        ms = 0.0
+        for it in range(2):  # the first transfer sets up the peer connection
+            _barrier(world)
+            if rank in (0, 1):
+                a.record()
+                if rank == 0:
+                    torch.distributed.send(buf, 1)
+                else:
+                    torch.distributed.recv(buf, 0)
+                b.record()
+                torch.cuda.synchronize()
+                ms = a.elapsed_time(b)
+            ms = _max_over_ranks(ms if rank in (0, 1) else 0.0, world, dev)
+        out["nvlink_p2p_gbps"] = round(nbytes / (ms / 1e3) / 1e9, 2)
+    del buf
+    torch.cuda.empty_cache()
+    out["bytes"] = nbytes
+    return out
+
+
+def allreduce_probe(world: int, dev, hidden: int, count: int, links: dict | None = None) -> dict | None:
     """The per-block exchange of tensor-parallel decoding: `count`
-    back-to-back all-reduces of one token's hidden state (BF16), timed with
-    CUDA events, max over ranks; bus bandwidth against the measured NVLink
-    peer-copy rate (latency-bound at this size)."""
+    back-to-back all-reduces of one token's fp32 row-parallel partial sums
+    (hidden floats), through NCCL and through the one-shot NVLink kernel the
+    decoder uses (runtime/allreduce.py), CUDA events, max over ranks.
+    Latency-bound at this size: the bus rate is far below the link rate."""
     if world < 2:
         return None
-    x = torch.randn(1, hidden, device=dev).to(torch.bfloat16)
-    for _ in range(20):
-        torch.distributed.all_reduce(x)
-    torch.cuda.synchronize()
-    _barrier(world)
+    from afterimage_b200.runtime.allreduce import OneShotAllReduce
+    x = torch.randn(hidden, device=dev)
+    ar = OneShotAllReduce(None, dev, hidden)
+    nbytes = hidden * 4
+    out = {"all_reduces_per_token": count, "bytes_each": nbytes}
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(count):
-        torch.distributed.all_reduce(x)
-    b.record()
-    torch.cuda.synchronize()
-    ms = _max_over_ranks(a.elapsed_time(b), world, dev)
-    per_us = ms * 1e3 / count
-    nbytes = hidden * 2
-    bus = 2 * (world - 1) / world * nbytes / (per_us * 1e-6) / 1e9
-    return {"all_reduces_per_token": count, "bytes_each": nbytes, "us_each": round(per_us, 2),
-            "bus_gbps": round(bus, 3), "nvlink_peak_gbps": 770.0, "frac": round(bus / 770.0, 6),
-            "note": "one token's hidden state per all-reduce: latency-bound, far below link bandwidth"}
+    for name, fn in (("nccl", lambda: torch.distributed.all_reduce(x)), ("oneshot", lambda: ar(x))):
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize()
+        _barrier(world)
+        a.record()
+        for _ in range(count):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms = _max_over_ranks(a.elapsed_time(b), world, dev)
+        per_us = ms * 1e3 / count
+        out[name] = {"us_each": round(per_us, 2), "ms_per_token": round(ms, 3),
+                     "bus_gbps": round(2 * (world - 1) / world * nbytes / (per_us * 1e-6) / 1e9, 3)}
+    ar.close()
+    if links and links.get("nvlink_p2p_gbps"):
+        out["nvlink_p2p_gbps_measured"] = links["nvlink_p2p_gbps"]
+    out["note"] = "one token's fp32 partial sums per all-reduce: latency-bound, far below the link rate"
+    return out
 
 
 def tp_store_chunk_size(world: int) -> int:
@@ -450,7 +499,8 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
     """Greedy tokens/s of the --model shape (default Qwen3-14B, the benchmark's 14B configuration) through
     the tensor-parallel decoder on `world` GPUs (one rank per GPU; world=1
     is a single GPU): every rank decodes only its own column/row shards of
-    every layer, one NCCL all-reduce after o_proj and after down_proj.
+    every layer, one all-reduce after o_proj and after down_proj (the
+    one-shot NVLink kernel; NCCL for sums above its buffer).
       streamed:            compressed shards in page-locked host memory,
                            copied to the GPU one layer at a time (the layer
                            streamer over PCIe; device memory stays a few GB);
@@ -497,6 +547,7 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
                                     resident="decoded")
         _barrier(world)
         prompt = torch.randint(0, cfg.vocab_size, (1, P), generator=torch.Generator().manual_seed(64))
+        links = link_rates(world, rank, dev)
         seqs = {}
         for name, resident, kw in (("streamed", "streamed", {}),
                                    ("streamed_%gGB_per_rank" % budget, "streamed",
@@ -547,11 +598,12 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
             # the terms that bound one single-token forward on this rank: PCIe for the
             # streamed bytes, HBM for the decode, HBM for the projections reading the
             # decoded BF16 weights; the largest is the tokens/s roofline
-            terms = {"pcie_ms": round(dec.h2d_bytes_per_forward() / PCIE_GBS / 1e6, 3),
+            pcie_gbs = links.get("pcie_h2d_gbps") or PCIE_GBS_FALLBACK
+            terms = {"pcie_ms": round(dec.h2d_bytes_per_forward() / pcie_gbs / 1e6, 3),
                      "decode_hbm_ms": round(dbytes / peak_hbm / 1e6, 3),
                      "projection_hbm_ms": round(2 * dec.weights_per_forward() / peak_hbm / 1e6, 3)}
             bound = max(terms, key=terms.get)
-            info["roofline_terms"] = dict(terms, bound=bound, pcie_gbs=PCIE_GBS, hbm_gbs=peak_hbm,
+            info["roofline_terms"] = dict(terms, bound=bound, pcie_gbs=pcie_gbs, hbm_gbs=peak_hbm,
                                           step_ms=round(step_ms, 3),
                                           frac_of_bound=round(terms[bound] / step_ms, 4) if step_ms else None)
             if resident != "streamed":
@@ -588,14 +640,21 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
                 up = tl.get("upload_busy_ms", 0.0)
                 info.update(h2d_bytes_per_forward_per_rank=hb,
                             h2d_gbps_in_step=round(hb / (up / 1e3) / 1e9, 1) if up else None)
-                dec.close()
+            if tl.get("allreduce_busy_ms") is not None and tl.get("span_ms"):
+                info["allreduce_share_of_step"] = round(tl["allreduce_busy_ms"] / tl["span_ms"], 4)
+            info["collective"] = "oneshot NVLink all-reduce" if dec.allreducer is not None else \
+                ("none" if world == 1 else "NCCL all-reduce")
+            dec.close()  # collective when the one-shot all-reduce is in use
             if rank == 0 and name == "compressed_resident":
                 (root / "timeline_events.json").write_text(json.dumps(events))
             out[name] = info
             del dec, cache
             torch.cuda.empty_cache()
         out["tokens_equal_across_modes"] = all(bool(torch.equal(v, seqs["compressed_resident"])) for v in seqs.values())
-        out["all_reduce"] = allreduce_probe(world, dev, cfg.hidden_size, 2 * cfg.num_hidden_layers)
+        out["all_reduce"] = allreduce_probe(world, dev, cfg.hidden_size, 2 * cfg.num_hidden_layers, links)
+        out["links"] = links
+        if draft is not None:
+            draft.close()
         return out
     finally:
         _barrier(world)

@@ -37,6 +37,7 @@ extern "C" {
 #define AIB_STATUS_LUT_NOT_PREFIX 2  /* tables: LUT is not a prefix-code table; decoded exactly via the slow path */
 #define AIB_STATUS_LUT_RANGE 4       /* tables: a symbol outside [0, 255] or a length outside [0, max_bits] */
 #define AIB_STATUS_WAIT_TIMEOUT 8    /* a bounded wait on a bulk copy gave up; the CTA returned early */
+#define AIB_STATUS_PEER_TIMEOUT 16   /* all-reduce: a bounded wait for a peer's flag gave up */
 
 /* Polls of the kernels' one device-side wait (the table's bulk copy, with a
  * short sleep between polls) before the CTA gives up with
@@ -325,6 +326,46 @@ int aib_recombine(const uint8_t *exponent, const uint8_t *sign_mantissa, int64_t
  * would. No copy is issued, so nothing outlives the CTA. Enqueued on
  * `stream`; no synchronisation. */
 int aib_selftest_wait_timeout(unsigned polls, int32_t *d_status, void *stream);
+
+/* ------------------------------------------------------------------------
+ * One-shot all-reduce over NVLink peer memory (tensor-parallel decoder:
+ * the row-parallel o_proj / down_proj partial sums). The reference runs on
+ * one GPU and has no counterpart; this replaces the NCCL all-reduce the
+ * tensor-parallel decoder would otherwise make.
+ *
+ * Each rank allocates one buffer (aib_ar_alloc), shares its IPC handle
+ * (aib_ar_ipc_handle, AIB_AR_HANDLE_BYTES bytes) with the other ranks of
+ * the node, opens theirs (aib_ar_ipc_open) and fills an aib_ar_group with
+ * every rank's buffer as mapped in this process. After a host barrier (the
+ * buffers start zeroed) every rank makes the same aib_allreduce_oneshot_f32
+ * calls in the same order: out = sum over ranks of in, fp32, added in rank
+ * order, so every rank gets bit-identical sums. in == out is allowed.
+ * Stream-ordered. A wait for a peer polls at most max_polls times (with
+ * backoff); when it gives up it sets AIB_STATUS_PEER_TIMEOUT in *d_status
+ * and the group must not be used again. Ranks of one group must run on
+ * different GPUs.
+ * ------------------------------------------------------------------------ */
+#define AIB_AR_MAX_RANKS 8
+#define AIB_AR_MAX_CTAS 64
+#define AIB_AR_HANDLE_BYTES 64
+typedef struct aib_ar_group {
+  void *buffers[AIB_AR_MAX_RANKS]; /* rank p's buffer as mapped here; [rank] is this rank's own */
+  int32_t rank;
+  int32_t world;                   /* 1 .. AIB_AR_MAX_RANKS */
+  int64_t max_floats;              /* the capacity every buffer was allocated with */
+} aib_ar_group;
+size_t aib_ar_buffer_bytes(int64_t max_floats);
+/* cudaMalloc of aib_ar_buffer_bytes(max_floats) on the current device,
+ * header zeroed; synchronises the device. */
+int aib_ar_alloc(int64_t max_floats, void **d_buffer);
+int aib_ar_free(void *d_buffer);
+int aib_ar_ipc_handle(void *d_buffer, void *handle_out);
+int aib_ar_ipc_open(const void *handle, void **d_peer);
+int aib_ar_ipc_close(void *d_peer);
+/* CTAs (and flag slots) a call of n floats uses. */
+int aib_ar_ctas(int64_t n);
+int aib_allreduce_oneshot_f32(const aib_ar_group *g, const float *in, float *out, int64_t n, unsigned max_polls,
+                              int32_t *d_status, void *stream);
 
 #ifdef __cplusplus
 }

@@ -39,7 +39,8 @@ def test_library_exports_nothing_else():
     assert extra == [], extra[:20]
 
 
-@pytest.mark.parametrize("ctype,cname", [(_lib.StreamDesc, "aib_stream_desc"), (_lib.GemvDesc, "aib_gemv_desc")])
+@pytest.mark.parametrize("ctype,cname", [(_lib.StreamDesc, "aib_stream_desc"), (_lib.GemvDesc, "aib_gemv_desc"),
+                                         (_lib.ArGroup, "aib_ar_group")])
 def test_descriptor_layout_matches_header_order(tmp_path, ctype, cname):
     """The ctypes descriptors must have the C compiler's size and field offsets."""
     import subprocess
