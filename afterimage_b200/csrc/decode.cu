@@ -69,7 +69,7 @@ namespace aib {
 
 // Tuning parameters (compile-time; -D overrides exist for sweeps).
 #ifndef AIB_WARPS
-#define AIB_WARPS 24
+#define AIB_WARPS 18
 #endif
 #ifndef AIB_PHASE
 #define AIB_PHASE 64
