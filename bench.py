@@ -455,8 +455,10 @@ def allreduce_probe(world: int, dev, hidden: int, count: int, links: dict | None
     """The per-block exchange of tensor-parallel decoding: `count`
     back-to-back all-reduces of one token's fp32 row-parallel partial sums
     (hidden floats), through NCCL and through the one-shot NVLink kernel the
-    decoder uses (runtime/allreduce.py), CUDA events, max over ranks.
-    Latency-bound at this size: the bus rate is far below the link rate."""
+    decoder uses (runtime/allreduce.py). Each is timed eagerly and as one
+    captured CUDA graph of the `count` calls (as the graphed decode step runs
+    them: no host launch cost), CUDA events, max over ranks. Latency-bound at
+    this size: the bus rate is far below the link rate."""
     if world < 2:
         return None
     from afterimage_b200.runtime.allreduce import OneShotAllReduce
@@ -465,6 +467,7 @@ def allreduce_probe(world: int, dev, hidden: int, count: int, links: dict | None
     nbytes = hidden * 4
     out = {"all_reduces_per_token": count, "bytes_each": nbytes}
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    side = torch.cuda.Stream(dev)
     for name, fn in (("nccl", lambda: torch.distributed.all_reduce(x)), ("oneshot", lambda: ar(x))):
         for _ in range(20):
             fn()
@@ -475,10 +478,33 @@ def allreduce_probe(world: int, dev, hidden: int, count: int, links: dict | None
             fn()
         b.record()
         torch.cuda.synchronize()
-        ms = _max_over_ranks(a.elapsed_time(b), world, dev)
-        per_us = ms * 1e3 / count
-        out[name] = {"us_each": round(per_us, 2), "ms_per_token": round(ms, 3),
-                     "bus_gbps": round(2 * (world - 1) / world * nbytes / (per_us * 1e-6) / 1e9, 3)}
+        eager_ms = _max_over_ranks(a.elapsed_time(b), world, dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            fn()  # warm on the capture stream
+        torch.cuda.synchronize()
+        _barrier(world)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(count):
+                fn()
+        torch.cuda.synchronize()
+        _barrier(world)
+        graph.replay()  # warm
+        torch.cuda.synchronize()
+        _barrier(world)
+        a.record()
+        graph.replay()
+        b.record()
+        torch.cuda.synchronize()
+        graph_ms = _max_over_ranks(a.elapsed_time(b), world, dev)
+        del graph  # graphs holding NCCL calls go before the process group
+        torch.cuda.synchronize()
+        per_us = graph_ms * 1e3 / count
+        out[name] = {"us_each_graphed": round(per_us, 2), "ms_per_token_graphed": round(graph_ms, 3),
+                     "us_each_eager": round(eager_ms * 1e3 / count, 2),
+                     "bus_gbps_graphed": round(2 * (world - 1) / world * nbytes / (per_us * 1e-6) / 1e9, 3)}
+    _barrier(world)
     ar.close()
     if links and links.get("nvlink_p2p_gbps"):
         out["nvlink_p2p_gbps_measured"] = links["nvlink_p2p_gbps"]
@@ -549,10 +575,13 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
         prompt = torch.randint(0, cfg.vocab_size, (1, P), generator=torch.Generator().manual_seed(64))
         links = link_rates(world, rank, dev)
         seqs = {}
-        for name, resident, kw in (("streamed", "streamed", {}),
-                                   ("streamed_%gGB_per_rank" % budget, "streamed",
-                                    {"vram_budget_gb": budget, "max_context": P + args.new_tokens + 8}),
-                                   ("compressed_resident", "compressed", {"overlap": True})):
+        modes = (("streamed", "streamed", {}),
+                 ("streamed_%gGB_per_rank" % budget, "streamed",
+                  {"vram_budget_gb": budget, "max_context": P + args.new_tokens + 8}),
+                 ("compressed_resident", "compressed", {"overlap": True}))
+        wanted = set((getattr(args, "tp_modes", None) or "streamed,streamed_budget,compressed_resident").split(","))
+        modes = [m for m in modes if (m[0] if not m[0].startswith("streamed_") else "streamed_budget") in wanted]
+        for name, resident, kw in modes:
             harness = torch.cuda.memory_allocated(dev)  # the harness's own buffers, not the decoder's
             t0 = time.perf_counter()
             dec = load_tp_decoder(store, cfg, world, rank, None, dev, resident=resident, **kw)
@@ -650,8 +679,12 @@ def run_tp_tokens(args, world: int, rank: int, dev) -> dict:
             out[name] = info
             del dec, cache
             torch.cuda.empty_cache()
-        out["tokens_equal_across_modes"] = all(bool(torch.equal(v, seqs["compressed_resident"])) for v in seqs.values())
-        out["all_reduce"] = allreduce_probe(world, dev, cfg.hidden_size, 2 * cfg.num_hidden_layers, links)
+        ref_seq = next(iter(seqs.values()))
+        out["tokens_equal_across_modes"] = all(bool(torch.equal(v, ref_seq)) for v in seqs.values())
+        try:
+            out["all_reduce"] = allreduce_probe(world, dev, cfg.hidden_size, 2 * cfg.num_hidden_layers, links)
+        except Exception as exc:  # reported; the tokens/s figures above stand
+            out["all_reduce"] = {"error": "%s: %s" % (type(exc).__name__, exc)}
         out["links"] = links
         if draft is not None:
             draft.close()
@@ -878,6 +911,11 @@ def main(argv=None) -> int:
     ap.add_argument("--projections", action="store_true",
                     help="instead of the benchmark: time one layer's projections (decode + cuBLAS, fused "
                          "decode->GEMV, this package's GEMV and tensor-core GEMM against cuBLAS)")
+    ap.add_argument("--tp-modes", default=None,
+                    help="comma list of tensor-parallel tokens/s modes to run (streamed, streamed_budget, "
+                         "compressed_resident; default all)")
+    ap.add_argument("--tp-tokens-only", action="store_true",
+                    help="run only the tensor-parallel tokens/s measurement of --model and print its JSON line")
     ap.add_argument("--no-tp-tokens", action="store_true",
                     help="skip the tensor-parallel tokens/s measurement (its store of the --model shape "
                          "is written to /dev/shm)")
@@ -898,6 +936,13 @@ def main(argv=None) -> int:
         if world > 1:
             torch.distributed.destroy_process_group()
         return rc
+    if args.tp_tokens_only:
+        t = run_tp_tokens(args, world, rank, dev)
+        if rank == 0:
+            print(json.dumps({"tokens_%s_tp" % args.model.replace("-", "_").replace(".", ""): t}), flush=True)
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return 0
     from afterimage_b200.runtime import layer_decode as LD
     from afterimage_b200.runtime import _device
 
