@@ -292,3 +292,47 @@ def test_tp_speculative_decoding_equals_greedy_on_gpu(stores, resident):
             assert st["accepted_from_draft"] >= 4 and st["sweeps"] <= 4
     if resident == "streamed":
         dec.close()
+
+
+def test_tp_wide_projections_on_own_kernels_match_transformers(tmp_path, monkeypatch):
+    """gate/up (2 x 8192 rows) and the head (16384 rows) are wide enough for
+    the fused mode to route them to this package's GEMV (up to 8 tokens) and
+    tcgen05 GEMM (9-64 tokens): logits for 1, 5, 11 and 70 tokens stay within
+    the BF16 tolerance of transformers, and both kernels are really used."""
+    from transformers import AutoModelForCausalLM, Qwen3Config
+    from afterimage_b200.runtime import tp_ops
+    from afterimage_b200.runtime.streaming_engine import write_store
+    from afterimage_b200.runtime.tp_decoder import TPDecoder, load_tp_decoder
+    torch.manual_seed(5)
+    cfg = Qwen3Config(vocab_size=16384, hidden_size=320, intermediate_size=8192, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, head_dim=80, max_position_embeddings=256,
+                      tie_word_embeddings=False)
+    model = AutoModelForCausalLM.from_config(cfg, dtype=torch.bfloat16)
+    with torch.no_grad():
+        for p in model.parameters():
+            if p.dim() == 2:
+                p.normal_(0, 0.02)
+    model = model.eval()
+    store = tmp_path / "wide"
+    write_store(((k, v.contiguous()) for k, v in model.state_dict().items()), store, tied=False)
+    assert 2 * cfg.intermediate_size >= TPDecoder.OWN_KERNEL_MIN_ROWS
+    calls = {"gemv": 0, "gemm_tc": 0}
+    for name in calls:
+        real = getattr(tp_ops, name)
+
+        def counted(*a, _real=real, _name=name, **k):
+            calls[_name] += 1
+            return _real(*a, **k)
+        monkeypatch.setattr(tp_ops, name, counted)
+    dec = load_tp_decoder(store, cfg, 1, 0, None, "cuda", resident="decoded")
+    model = model.to("cuda")
+    g = torch.Generator(device="cuda").manual_seed(9)
+    for T in (5, 11, 70):
+        ids = torch.randint(0, cfg.vocab_size, (1, T), device="cuda", generator=g)
+        with torch.no_grad():
+            ref = model(input_ids=ids).logits[0].float()
+        check_logits(dec.forward(ids).float(), ref)
+    assert calls["gemv"] > 0 and calls["gemm_tc"] > 0
+    # single-token steps after an 11-token prompt (fused layer kernels + GEMV)
+    ids = torch.randint(0, cfg.vocab_size, (1, 11), device="cuda", generator=g)
+    _check_single_token_steps(dec, model, ids, 4)
