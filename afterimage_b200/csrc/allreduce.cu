@@ -8,25 +8,24 @@
 // the node through CUDA IPC handles):
 //   [0, 8)           the call counter (epoch) and a count of finished CTAs
 //                    (local use only)
-//   [4 KiB, 8 KiB)   flags[src_rank][cta] (int32), written by the peers
-//   [8 KiB, ...)     data[2][max_floats] (fp32), two parities
-// Call e on every rank (the same calls in the same order on every rank),
-// CTA b of G (G fixed by n, so the same on every rank):
-//   1. copy the rank's slice b of `in` into its own data[e & 1];
-//   2. fence (system scope), then store e into flags[rank][b] of every rank;
-//   3. wait, bounded, until its own flags[p][b] >= e for every rank p;
-//   4. out[slice b] = sum over p = 0 .. world-1, in that order, of slice b
-//      of data[e & 1] of rank p (NVLink loads): the same order on every
-//      rank, so all ranks hold bit-identical sums;
-//   5. the last CTA to finish advances the epoch to e.
-// A rank writes data[e & 1] again only in call e + 2. Before that, its call
-// e + 1 saw a flag of call e + 1 from every peer; a peer's call e + 1 starts
-// after its whole call e (stream order), reads included. So two parities
-// suffice, with no second barrier, whatever G each call uses.
-// A wait that gives up sets AIB_STATUS_PEER_TIMEOUT in the status word and
-// the CTA returns without touching `out` (the group is then unusable; the
-// host raises and tears it down). No load here uses TMA or cluster
-// multicast; peers are read with plain vector loads that bypass L1.
+//   [4 KiB, ...)     recv[2][AIB_AR_MAX_RANKS][max_floats] of 64-bit words,
+//                    two parities, written by the peers
+// Call e on every rank (the same calls in the same order on every rank):
+// element i of this rank's input goes to every peer as ONE 64-bit store of
+// (value bits, e) into the peer's recv[e & 1][rank][i]. A receiver polls its
+// own recv[e & 1][p][i] until the word carries e, and then holds the value:
+// a single-copy-atomic 64-bit store cannot be seen half written, so no
+// fence and no separate flag are needed and a value costs one one-way
+// NVLink write. out[i] is the sum over p = 0 .. world-1, in that order (the
+// rank's own value from `in`), so every rank holds bit-identical sums.
+// A rank writes recv[e & 1][rank] of a peer again only in call e + 2. Its
+// call e + 1 waited for that peer's words of call e + 1, which the peer
+// wrote after its whole call e (stream order), reads included. So two
+// parities suffice with no second barrier. The last CTA of a call advances
+// the epoch, so the kernel runs unchanged inside a CUDA graph.
+// A wait that gives up sets AIB_STATUS_PEER_TIMEOUT in the status word (the
+// group is then unusable; the host raises and tears it down). No load here
+// uses TMA or cluster multicast; peers are only written, with plain stores.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -40,104 +39,85 @@ namespace aibar {
 constexpr int kThreads = 256;
 constexpr int kMaxCtas = AIB_AR_MAX_CTAS;
 constexpr int64_t kCounterOff = 0;
-constexpr int64_t kFlagOff = 4096;
-constexpr int64_t kDataOff = 8192;
-static_assert(AIB_AR_MAX_RANKS * kMaxCtas * 4 <= 4096, "flag block size");
+constexpr int64_t kRecvOff = 4096;
 
 struct Args {
-  float *data[AIB_AR_MAX_RANKS];     // each rank's data[0] as mapped here
-  int32_t *flags[AIB_AR_MAX_RANKS];  // each rank's flag block as mapped here
+  uint64_t *recv[AIB_AR_MAX_RANKS];  // each rank's recv[0][0] as mapped here
   int32_t *counters;                 // this rank's {epoch, finished CTAs}
-  int64_t max_floats;
+  int64_t max_floats;                // words per (parity, source) row
   int32_t rank, world;
 };
 
-__device__ __forceinline__ void st_release_sys(int32_t *p, int32_t v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_relaxed_sys(uint64_t *p, uint64_t v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-__device__ __forceinline__ int32_t ld_acquire_sys(const int32_t *p) {
-  int32_t v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ uint64_t ld_relaxed_sys(const uint64_t *p) {
+  uint64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
 
 __global__ void __launch_bounds__(kThreads) oneshot_kernel(const Args a, const float *in, float *out, int64_t n,
-                                                           int vec, unsigned max_polls, int32_t *status) {
+                                                           unsigned max_polls, int32_t *status) {
   __shared__ int32_t s_ep;
   __shared__ int s_fail;
-  const int b = blockIdx.x;
-  const int64_t per = ((n + gridDim.x - 1) / gridDim.x + 3) / 4 * 4;
-  const int64_t lo = min(n, per * b);
-  const int64_t hi = min(n, lo + per);
   if (threadIdx.x == 0) {
     s_ep = a.counters[0] + 1;
     s_fail = 0;
   }
   __syncthreads();
-  const int32_t ep = s_ep;
-  const int64_t par = static_cast<int64_t>(ep & 1) * a.max_floats;
-  float *mine = a.data[a.rank] + par;
+  const uint32_t ep = static_cast<uint32_t>(s_ep);
+  const int64_t row = a.max_floats;
+  const int64_t par = static_cast<int64_t>(ep & 1u) * AIB_AR_MAX_RANKS * row;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kThreads;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * kThreads + threadIdx.x;
 
-  // 1. this rank's slice into its own buffer
-  if (vec) {
-    for (int64_t i = lo + 4 * threadIdx.x; i < hi; i += 4 * kThreads)
-      *reinterpret_cast<float4 *>(mine + i) = *reinterpret_cast<const float4 *>(in + i);
-  } else {
-    for (int64_t i = lo + threadIdx.x; i < hi; i += kThreads) mine[i] = in[i];
+  // 1. every element to every peer: (value bits, epoch) in one 64-bit store
+  for (int64_t i = first; i < n; i += stride) {
+    const uint64_t w = static_cast<uint64_t>(__float_as_uint(in[i])) | (static_cast<uint64_t>(ep) << 32);
+    for (int p = 0; p < a.world; ++p)
+      if (p != a.rank) st_relaxed_sys(a.recv[p] + par + a.rank * row + i, w);
   }
-  __threadfence_system();
-  __syncthreads();
 
-  // 2. announce call ep to every rank (itself included), 3. wait for theirs
-  if (threadIdx.x < a.world) {
-    const int p = threadIdx.x;
-    st_release_sys(a.flags[p] + a.rank * kMaxCtas + b, ep);
-    const int32_t *f = a.flags[a.rank] + p * kMaxCtas + b;
-    unsigned polls = 0;
-    while (ld_acquire_sys(f) - ep < 0) {
-      if (++polls > max_polls) {
-        atomicOr(&s_fail, 1);
-        break;
+  // 2. wait for each peer's word of each element, sum in rank order
+  const uint64_t *mine = a.recv[a.rank] + par;
+  bool fail = false;
+  for (int64_t i = first; i < n && !fail; i += stride) {
+    float s = 0.f;
+    for (int p = 0; p < a.world; ++p) {
+      float x;
+      if (p == a.rank) {
+        x = in[i];
+      } else {
+        const uint64_t *q = mine + p * row + i;
+        uint64_t w = ld_relaxed_sys(q);
+        unsigned polls = 0;
+        while (static_cast<uint32_t>(w >> 32) != ep) {
+          if (++polls > max_polls) {
+            fail = true;
+            break;
+          }
+          if (polls > 4096) __nanosleep(64);
+          w = ld_relaxed_sys(q);
+        }
+        if (fail) break;
+        x = __uint_as_float(static_cast<uint32_t>(w));
       }
-      if (polls > 2048) __nanosleep(128);
+      s = p == 0 ? x : s + x;
     }
+    if (!fail) out[i] = s;
   }
-  __syncthreads();
-  if (s_fail) {
-    if (threadIdx.x == 0 && status) atomicOr(status, AIB_STATUS_PEER_TIMEOUT);
-    return;
-  }
-  __threadfence_system();
-
-  // 4. the sum in rank order
-  if (vec) {
-    for (int64_t i = lo + 4 * threadIdx.x; i < hi; i += 4 * kThreads) {
-      float4 s = __ldcv(reinterpret_cast<const float4 *>(a.data[0] + par + i));
-      for (int p = 1; p < a.world; ++p) {
-        const float4 v = __ldcv(reinterpret_cast<const float4 *>(a.data[p] + par + i));
-        s.x += v.x;
-        s.y += v.y;
-        s.z += v.z;
-        s.w += v.w;
-      }
-      *reinterpret_cast<float4 *>(out + i) = s;
-    }
-  } else {
-    for (int64_t i = lo + threadIdx.x; i < hi; i += kThreads) {
-      float s = __ldcv(a.data[0] + par + i);
-      for (int p = 1; p < a.world; ++p) s += __ldcv(a.data[p] + par + i);
-      out[i] = s;
-    }
-  }
-  // 5. the last CTA of the call advances the epoch (read by the next call
-  // on this stream, which starts after every CTA of this one)
+  if (fail) atomicOr(&s_fail, 1);
   __syncthreads();
   if (threadIdx.x == 0) {
+    if (s_fail && status) atomicOr(status, AIB_STATUS_PEER_TIMEOUT);
+    // 3. the last CTA of the call advances the epoch (read by the next call
+    // on this stream, which starts after every CTA of this one)
     __threadfence();
     if (atomicAdd(a.counters + 1, 1) == static_cast<int>(gridDim.x) - 1) {
       a.counters[1] = 0;
-      a.counters[0] = ep;
+      a.counters[0] = static_cast<int32_t>(ep);
     }
   }
 }
@@ -148,14 +128,15 @@ using namespace aibar;
 
 AIB_API size_t aib_ar_buffer_bytes(int64_t max_floats) {
   if (max_floats < 0) return 0;
-  return static_cast<size_t>(kDataOff + 2 * 4 * ((max_floats + 3) / 4 * 4));
+  return static_cast<size_t>(kRecvOff + 2 * AIB_AR_MAX_RANKS * 8 * max_floats);
 }
 
 AIB_API int aib_ar_alloc(int64_t max_floats, void **d_buffer) {
   if (!d_buffer || max_floats < 1) return aib_set_error("aib_ar_alloc: bad arguments"), AIB_EINVAL;
   void *p = nullptr;
   cudaError_t e = cudaMalloc(&p, aib_ar_buffer_bytes(max_floats));
-  if (e == cudaSuccess) e = cudaMemset(p, 0, kDataOff);
+  // all of it zeroed: a word whose high half equals a call's epoch is data
+  if (e == cudaSuccess) e = cudaMemset(p, 0, aib_ar_buffer_bytes(max_floats));
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) {
     if (p) cudaFree(p);
@@ -202,7 +183,7 @@ AIB_API int aib_ar_ipc_close(void *d_peer) {
 
 AIB_API int aib_ar_ctas(int64_t n) {
   if (n <= 0) return 0;
-  return static_cast<int>(std::min<int64_t>(kMaxCtas, std::max<int64_t>(1, (n + 4095) / 4096)));
+  return static_cast<int>(std::min<int64_t>(kMaxCtas, std::max<int64_t>(1, (n + 1023) / 1024)));
 }
 
 AIB_API int aib_allreduce_oneshot_f32(const aib_ar_group *g, const float *in, float *out, int64_t n,
@@ -225,17 +206,13 @@ AIB_API int aib_allreduce_oneshot_f32(const aib_ar_group *g, const float *in, fl
     if (!g->buffers[p] || reinterpret_cast<uintptr_t>(g->buffers[p]) % 256)
       return aib_set_errorf("aib_allreduce_oneshot_f32: buffer of rank %d is null or not 256-byte aligned", p),
              AIB_EINVAL;
-    unsigned char *base = static_cast<unsigned char *>(g->buffers[p]);
-    a.data[p] = reinterpret_cast<float *>(base + kDataOff);
-    a.flags[p] = reinterpret_cast<int32_t *>(base + kFlagOff);
+    a.recv[p] = reinterpret_cast<uint64_t *>(static_cast<unsigned char *>(g->buffers[p]) + kRecvOff);
   }
   a.counters = reinterpret_cast<int32_t *>(static_cast<unsigned char *>(g->buffers[g->rank]) + kCounterOff);
-  a.max_floats = (g->max_floats + 3) / 4 * 4;
+  a.max_floats = g->max_floats;
   a.rank = g->rank;
   a.world = g->world;
-  const int vec =
-      n % 4 == 0 && reinterpret_cast<uintptr_t>(in) % 16 == 0 && reinterpret_cast<uintptr_t>(out) % 16 == 0;
-  oneshot_kernel<<<aib_ar_ctas(n), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, in, out, n, vec, max_polls,
+  oneshot_kernel<<<aib_ar_ctas(n), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, in, out, n, max_polls,
                                                                                       d_status);
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return aib_set_errorf("aib_allreduce_oneshot_f32: %s", cudaGetErrorString(e)), AIB_ECUDA;

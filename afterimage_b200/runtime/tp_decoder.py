@@ -331,7 +331,7 @@ class TPDecoder:
         return w() if callable(w) else w
 
     # -- collectives ----------------------------------------------------------
-    def use_oneshot_allreduce(self, max_floats: int = 1 << 20) -> None:
+    def use_oneshot_allreduce(self, max_floats: int = 1 << 16) -> None:
         """Collective (every rank calls it): the row-parallel sums of up to
         max_floats floats go through the one-shot NVLink all-reduce
         (runtime/allreduce.py, csrc/allreduce.cu) instead of NCCL; larger

@@ -354,15 +354,17 @@ typedef struct aib_ar_group {
   int32_t world;                   /* 1 .. AIB_AR_MAX_RANKS */
   int64_t max_floats;              /* the capacity every buffer was allocated with */
 } aib_ar_group;
+/* 4 KiB + 2 x AIB_AR_MAX_RANKS x 8 bytes x max_floats: every element
+ * travels as one 64-bit (value, call number) word per rank and parity. */
 size_t aib_ar_buffer_bytes(int64_t max_floats);
 /* cudaMalloc of aib_ar_buffer_bytes(max_floats) on the current device,
- * header zeroed; synchronises the device. */
+ * zeroed; synchronises the device. */
 int aib_ar_alloc(int64_t max_floats, void **d_buffer);
 int aib_ar_free(void *d_buffer);
 int aib_ar_ipc_handle(void *d_buffer, void *handle_out);
 int aib_ar_ipc_open(const void *handle, void **d_peer);
 int aib_ar_ipc_close(void *d_peer);
-/* CTAs (and flag slots) a call of n floats uses. */
+/* CTAs a call of n floats uses. */
 int aib_ar_ctas(int64_t n);
 int aib_allreduce_oneshot_f32(const aib_ar_group *g, const float *in, float *out, int64_t n, unsigned max_polls,
                               int32_t *d_status, void *stream);

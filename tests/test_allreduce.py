@@ -1,8 +1,8 @@
 """One-shot NVLink all-reduce (csrc/allreduce.cu, runtime/allreduce.py).
 
 Host-side validation runs without a GPU. On one GPU: a single-rank group
-is a copy, and a two-rank group whose second rank never arrives (its flag
-is never raised) gives up within its poll limit with AIB_STATUS_PEER_TIMEOUT,
+is a copy, and a two-rank group whose second rank never arrives (its words
+never land) gives up within its poll limit with AIB_STATUS_PEER_TIMEOUT,
 leaving the context usable. On two GPUs (one process each, NCCL for the
 handle exchange): sums bit-identical to an explicit rank-order fp32 sum of
 the gathered inputs on every rank, across sizes, repeated calls and CUDA
@@ -47,9 +47,9 @@ def test_host_validation_without_a_gpu():
 
 def test_buffer_size_and_grid():
     L = _lib.load()
-    assert L.aib_ar_buffer_bytes(1) == 8192 + 2 * 4 * 4
-    assert L.aib_ar_buffer_bytes(1 << 20) == 8192 + 8 * (1 << 20)
-    assert [L.aib_ar_ctas(n) for n in (0, 1, 4096, 4097, 5120, 1 << 20, 1 << 30)] == [0, 1, 1, 2, 2, 64, 64]
+    assert L.aib_ar_buffer_bytes(1) == 4096 + 2 * 8 * 8
+    assert L.aib_ar_buffer_bytes(1 << 16) == 4096 + 128 * (1 << 16)
+    assert [L.aib_ar_ctas(n) for n in (0, 1, 1024, 1025, 5120, 1 << 20, 1 << 30)] == [0, 1, 1, 2, 5, 64, 64]
 
 
 def test_cpu_decoder_keeps_its_collective():
@@ -88,8 +88,9 @@ def test_single_rank_is_a_copy_and_in_place_works():
 
 @pytest.mark.gpu
 def test_a_peer_that_never_arrives_times_out_with_a_status():
-    """Rank 1's buffer is this rank's own, and nothing raises rank 1's flag:
-    the one kernel's bounded wait gives up (no second launch waits on it)."""
+    """Rank 1's buffer is this rank's own, and nothing writes rank 1's
+    words: the one kernel's bounded wait gives up (no second launch waits on
+    it)."""
     from afterimage_b200.runtime import _device
     L = _lib.load()
     dev = torch.device("cuda", 0)
