@@ -108,6 +108,7 @@ SIGNATURES = [
     ("aib_decode_exponents_u8", CI, [ctypes.POINTER(StreamDesc), P, P]),
     ("aib_decode_exponents_i32", CI, [ctypes.POINTER(StreamDesc), P, P]),
     ("aib_decode_bf16_batch", CI, [ctypes.POINTER(StreamDesc), CI, P, P]),
+    ("aib_decode_bf16_batch_ctas", CI, [ctypes.POINTER(StreamDesc), CI, CI, P, P]),
     ("aib_decode_gemv_bf16_batch", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
     ("aib_decode_gemv_bf16_batch_noalloc", CI, [ctypes.POINTER(GemvDesc), CI, P, P]),
     ("aib_recombine", CI, [P, P, I64, P, P]),

@@ -1151,8 +1151,10 @@ static void apportion(int64_t cap, const int64_t *groups, const int64_t *max_use
   }
 }
 
+// max_ctas > 0 caps the grid (one CTA holds one SM): the warps then loop
+// over more groups each and the SMs left over run other streams' kernels.
 template <int MODE>
-static int launch(const aib_stream_desc *descs, int count, int32_t *status, void *stream) {
+static int launch(const aib_stream_desc *descs, int count, int32_t *status, void *stream, int max_ctas = 0) {
   if (count < 1 || count > AIB_MAX_BATCH) {
     aib_set_errorf("batch count must be in [1, %d], got %d", AIB_MAX_BATCH, count);
     return AIB_EINVAL;
@@ -1182,7 +1184,8 @@ static int launch(const aib_stream_desc *descs, int count, int32_t *status, void
   const int64_t wave = static_cast<int64_t>(di->sms) * di->occ[MODE];
   int64_t want = (total_groups + kWarps * kGroupsPerWarp - 1) / (kWarps * kGroupsPerWarp);
   if (AIB_SPREAD) want = std::max(want, std::min(total_groups, wave));
-  const int64_t cap = std::min<int64_t>(std::max<int64_t>(want, 1), kMaxWaves * wave);
+  int64_t cap = std::min<int64_t>(std::max<int64_t>(want, 1), kMaxWaves * wave);
+  if (max_ctas > 0) cap = std::min<int64_t>(cap, max_ctas);
   int64_t groups[AIB_MAX_BATCH], max_useful[AIB_MAX_BATCH];
   int32_t share[AIB_MAX_BATCH];
   for (int i = 0; i < n; ++i) {
@@ -1361,6 +1364,12 @@ AIB_API int aib_decode_exponents_u8(const aib_stream_desc *desc, int32_t *d_stat
 
 AIB_API int aib_decode_exponents_i32(const aib_stream_desc *desc, int32_t *d_status, void *stream) {
   return launch<kModeI32>(desc, 1, d_status, stream);
+}
+
+AIB_API int aib_decode_bf16_batch_ctas(const aib_stream_desc *descs, int count, int max_ctas, int32_t *d_status,
+                                       void *stream) {
+  if (max_ctas < 1) return aib_set_errorf("max_ctas must be >= 1, got %d", max_ctas), AIB_EINVAL;
+  return launch<kModeBF16>(descs, count, d_status, stream, max_ctas);
 }
 
 AIB_API int aib_decode_bf16_batch(const aib_stream_desc *descs, int count, int32_t *d_status, void *stream) {

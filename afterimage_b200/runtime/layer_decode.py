@@ -119,9 +119,12 @@ class LayerDecoder:
     """Decodes lists of resident (or host) compressed tensors, up to
     AIB_MAX_BATCH per kernel launch, on torch.cuda.current_stream(device)."""
 
-    def __init__(self, device="cuda"):
+    def __init__(self, device="cuda", max_ctas: int = 0):
         self.device = _device.cuda_device(device)
         self.launches = 0
+        # > 0: each launch uses at most this many CTAs (one per SM), leaving
+        # the other SMs to kernels on other streams (aib_decode_bf16_batch_ctas)
+        self.max_ctas = int(max_ctas)
 
     def descriptors(self, tensors: list[ResidentLayer], outs: list[torch.Tensor]):
         descs = (_lib.StreamDesc * len(tensors))()
@@ -129,17 +132,23 @@ class LayerDecoder:
             descs[i] = _device.make_desc(r.stream, r.tables, r.encoded, 0, r.n, o, r.sign_mantissa)
         return descs
 
-    def launch(self, descs, count: int) -> None:
-        """One batched decode launch over prepared descriptors."""
+    def launch(self, descs, count: int, max_ctas: int | None = None) -> None:
+        """One batched decode launch over prepared descriptors (at most
+        `max_ctas` CTAs when given, else self.max_ctas; 0 = no cap)."""
         L = _lib.load()
+        cap = self.max_ctas if max_ctas is None else int(max_ctas)
         with torch.cuda.device(self.device):
             for s in range(0, count, _lib.AIB_MAX_BATCH):
                 k = min(_lib.AIB_MAX_BATCH, count - s)
                 base = _lib.ctypes.addressof(descs) + s * _lib.ctypes.sizeof(_lib.StreamDesc)
-                _lib.check(L.aib_decode_bf16_batch(
-                    _lib.ctypes.cast(base, _lib.ctypes.POINTER(_lib.StreamDesc)), k,
-                    _device.status_word(self.device).data_ptr(), _device.stream_ptr(self.device)),
-                    "decode_bf16_batch")
+                ptr = _lib.ctypes.cast(base, _lib.ctypes.POINTER(_lib.StreamDesc))
+                status = _device.status_word(self.device).data_ptr()
+                if cap > 0:
+                    _lib.check(L.aib_decode_bf16_batch_ctas(ptr, k, cap, status,
+                                                            _device.stream_ptr(self.device)), "decode_bf16_batch_ctas")
+                else:
+                    _lib.check(L.aib_decode_bf16_batch(ptr, k, status, _device.stream_ptr(self.device)),
+                               "decode_bf16_batch")
                 self.launches += 1
 
     def decode(self, tensors: list[ResidentLayer], outs: list[torch.Tensor] | None = None) -> list[torch.Tensor]:

@@ -868,11 +868,14 @@ class CompressedTPDecoder(TPDecoder):
     The head (vocab rows of lm_head, or of a tied embedding) stays compressed
     in HBM and is decoded `head_block_rows` rows at a time into one reused
     buffer, so it never exists decoded in full. With `overlap`, layer i+1 is
-    decoded on a side stream while layer i's projections run."""
+    decoded on a side stream while layer i's projections run; `decode_sms`
+    (> 0) caps that decode's CTAs (one per SM) so that the projections get
+    the remaining SMs instead of queueing behind it."""
 
     def __init__(self, hf_cfg, weights: dict, streams: dict, world=1, rank=0, group=None, device="cuda",
                  mode: str = "compressed", slots: int = 3, head_block_rows: int = 16384, overlap: bool = False,
-                 fused: bool = True, vram_budget_gb: float | None = None, max_context: int = 4096):
+                 fused: bool = True, vram_budget_gb: float | None = None, max_context: int = 4096,
+                 decode_sms: int | None = None):
         super().__init__(hf_cfg, weights, world, rank, group, device, fused=fused)
         if mode not in ("compressed", "streamed"):
             raise ValueError("mode must be 'compressed' or 'streamed'")
@@ -899,6 +902,13 @@ class CompressedTPDecoder(TPDecoder):
         self._desc_cache: dict = {}
         self.overlap = bool(overlap)
         self._dec_stream = torch.cuda.Stream(self.dev) if self.overlap else None
+        # with overlap: SMs the side-stream layer decode may hold (0 = all); the
+        # rest stay free for the current layer's projections. The default, 78 %
+        # of the SMs, is the best of a sweep of the 14B shape's graphed step at
+        # TP=1 on B200 (116 of 148 SMs: 18.1 -> 16.6 ms; 92 SMs: 20.7 ms)
+        if decode_sms is None:
+            decode_sms = round(0.78 * torch.cuda.get_device_properties(self.dev).multi_processor_count)
+        self.decode_sms = int(decode_sms) if self.overlap else 0
         self._ahead: dict = {}
         # decoded weights land in preallocated output sets (two when the decode of layer
         # i+1 overlaps layer i's projections), so descriptors are built once per
@@ -1056,7 +1066,7 @@ class CompressedTPDecoder(TPDecoder):
             descs, views = self._layer_plan(i, slot, oset)
             if segs:
                 t0 = _mark(stream) if self.timeline is not None else None
-                self.decoder.launch(descs, len(segs))
+                self.decoder.launch(descs, len(segs), max_ctas=self.decode_sms)
                 if t0 is not None:
                     self.timeline.append(("decode", i, t0, _mark(stream)))
             self._release_image(slot, stream)

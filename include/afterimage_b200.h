@@ -205,6 +205,13 @@ int aib_decode_exponents_i32(const aib_stream_desc *desc, int32_t *d_status, voi
  * 1 <= count <= AIB_MAX_BATCH. */
 #define AIB_MAX_BATCH 16
 int aib_decode_bf16_batch(const aib_stream_desc *descs, int count, int32_t *d_status, void *stream);
+/* The same launch on at most max_ctas CTAs (>= 1; one CTA holds one SM; a
+ * job still gets at least one CTA). The decode then leaves SMs to kernels
+ * of other streams: the tensor-parallel decoder decodes layer i + 1 on a
+ * side stream this way while layer i's projections run. No counterpart in
+ * the reference, which decodes and multiplies one after the other. */
+int aib_decode_bf16_batch_ctas(const aib_stream_desc *descs, int count, int max_ctas, int32_t *d_status,
+                               void *stream);
 
 /* Fused decode -> GEMV for one input vector (a single-token projection):
  * y = W x with W given only in compressed form. `stream` describes the

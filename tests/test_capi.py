@@ -199,3 +199,10 @@ def test_decode_tables_unpack_like_the_reference_pair():
     a, b = t
     assert isinstance(t, tuple) and len(t) == 2 and a is sym and b is ln
     assert t.block is blk and t.max_bits == 3 and t.sym_lut is sym and t.len_lut is ln
+
+
+def test_capped_batch_decode_rejects_a_zero_cap_without_a_gpu():
+    L = _lib.load()
+    d = _lib.StreamDesc()
+    assert L.aib_decode_bf16_batch_ctas(ctypes.byref(d), 1, 0, None, None) == _lib.AIB_EINVAL
+    assert b"max_ctas" in L.aib_last_error()

@@ -420,3 +420,27 @@ def test_recombine_entry_point_matches_oracle():
     got2 = recombine_exponent_and_sign_mantissa(torch.from_numpy(e)[1:], torch.from_numpy(sm)[1:],
                                                 (100_000,), "cuda")
     assert np.array_equal(_bits(got2).view(np.uint16), O.recombine(e[1:], sm[1:]))
+
+
+@pytest.mark.parametrize("max_ctas", [1, 3, 7, 100])
+def test_batch_decode_on_capped_ctas_is_bit_exact(max_ctas):
+    """aib_decode_bf16_batch_ctas: the same batch on at most max_ctas CTAs
+    (each job keeps at least one; its warps loop over more chunk groups)."""
+    from afterimage_b200.runtime import _device
+    from afterimage_b200.runtime.compressed_store import compress_layer
+    from afterimage_b200.runtime.layer_decode import LayerDecoder, upload_layer
+    dev = torch.device("cuda", 0)
+    shapes, chunks = [(512, 2048), (64, 2048), (2048, 640), (9, 5)], [1024, 1024, 640, 3]
+    Ws = []
+    for i, s in enumerate(shapes):
+        g = torch.Generator().manual_seed(70 + i)
+        Ws.append((torch.randn(*s, generator=g) * 0.02).to(torch.bfloat16))
+    resident = [upload_layer(compress_layer(W, chunk_size=c), dev, striped=(i % 2 == 0))
+                for i, (W, c) in enumerate(zip(Ws, chunks))]
+    dec = LayerDecoder(dev, max_ctas=max_ctas)
+    outs = dec.decode(resident)
+    torch.cuda.synchronize()
+    _device.check_status(dev)
+    assert dec.launches == 1
+    for W, o in zip(Ws, outs):
+        assert torch.equal(o.cpu().view(torch.int16), W.view(torch.int16))
