@@ -5,9 +5,10 @@ The reference engine runs on one GPU (its layers call nn.Linear on whole
 weights, afterimage/runtime/streaming_engine.py:1871-1915), so there is no
 reference collective; the alternative here is NCCL's all-reduce. For the
 small vectors of a decode step (one token: hidden_size floats) a call is
-one kernel: every rank writes its partial sums into its own buffer, raises
-a flag in every peer's buffer, and, once all flags are up, sums the ranks'
-buffers in rank order over NVLink. Every rank gets bit-identical sums.
+one kernel: every rank writes each of its partial sums, paired with the
+call's number in one 64-bit word, into every peer's receive buffer over
+NVLink, then waits in its own buffer for the peers' words of this call and
+sums the ranks' values in rank order. Every rank gets bit-identical sums.
 
 Setup is collective: `OneShotAllReduce(group, device, max_floats)` allocates
 this rank's buffer, exchanges CUDA IPC handles through the process group
@@ -40,6 +41,12 @@ class OneShotAllReduce:
             raise ValueError(f"one-shot all-reduce supports 1..{_lib.AR_MAX_RANKS} ranks, got {self.world}")
         self.max_floats = int(max_floats)
         self.max_polls = int(max_polls)
+        # the ranks' kernels wait on one another: they must run on different GPUs
+        uuids = [None] * self.world
+        with torch.cuda.device(self.device):
+            dist.all_gather_object(uuids, str(torch.cuda.get_device_properties(self.device).uuid), group=group)
+        if len(set(uuids)) != self.world:
+            raise ValueError("one-shot all-reduce needs one GPU per rank; ranks share a GPU")
         L = _lib.load()
         self._L = L
         self._own = ctypes.c_void_p()

@@ -340,7 +340,10 @@ class TPDecoder:
         if self.world < 2 or self.device.type != "cuda" or self.allreducer is not None:
             return
         from .allreduce import OneShotAllReduce
-        self.allreducer = OneShotAllReduce(self.group, self.device, max_floats)
+        try:
+            self.allreducer = OneShotAllReduce(self.group, self.device, max_floats)
+        except ValueError:  # ranks that share a GPU keep NCCL (every rank sees the same answer)
+            self.allreducer = None
 
     def _all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         if self.world > 1:
