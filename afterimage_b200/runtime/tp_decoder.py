@@ -1200,6 +1200,9 @@ def load_tp_decoder(store_dir, hf_cfg, world: int = 1, rank: int = 0, group=None
     from .compressed_store import decompress_layer_gpu
     if resident not in ("decoded", "compressed", "streamed"):
         raise ValueError("resident must be 'decoded', 'compressed' or 'streamed'")
+    collective = kw.pop("collective", "oneshot")
+    if collective not in ("oneshot", "nccl"):
+        raise ValueError("collective must be 'oneshot' or 'nccl'")
     store = pathlib.Path(store_dir)
     manifest = json.loads((store / "manifest.json").read_text())
     dev = _device.cuda_device(device)
@@ -1242,9 +1245,6 @@ def load_tp_decoder(store_dir, hf_cfg, world: int = 1, rank: int = 0, group=None
             weights[key] = ss.finish(decompress_layer_gpu(ss.layer, device=dev))
     if "lm_head.weight" not in weights and not getattr(hf_cfg, "tie_word_embeddings", False):
         raise RuntimeError("store has no lm_head.weight and the model is not tied")
-    collective = kw.pop("collective", "oneshot")
-    if collective not in ("oneshot", "nccl"):
-        raise ValueError("collective must be 'oneshot' or 'nccl'")
     if keep_compressed:
         dec = CompressedTPDecoder(hf_cfg, weights, streams, world, rank, group, dev,
                                   mode="streamed" if resident == "streamed" else "compressed", **kw)

@@ -211,3 +211,11 @@ def test_two_gpus_bit_identical_to_rank_order_sum():
             assert exact, (rank, n)
             assert diff_nccl <= 1e-6 * max(scale, 1.0), (rank, n, diff_nccl)
         assert all(graph_ok) and len(graph_ok) == 9
+
+
+def test_loader_rejects_an_unknown_collective(tmp_path):
+    """load_tp_decoder validates `collective` before building anything."""
+    from afterimage_b200.runtime.tp_decoder import load_tp_decoder
+    (tmp_path / "manifest.json").write_text('{"tensors": {}}')
+    with pytest.raises(ValueError, match="collective"):
+        load_tp_decoder(tmp_path, None, 1, 0, None, "cpu", resident="decoded", collective="mpi")
